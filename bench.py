@@ -1,0 +1,534 @@
+"""Benchmark of the MatMul16 / VecAdd path on B200s (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workload (weak scaling, fixed work per GPU): the row-sharded GEMM
+C = A.B + C with fp16 A, B and fp32 C.  Rank g owns rows [8192 g, 8192 (g+1))
+of A and C, B (K x N) is replicated; M = 8192 N, N = K = 8192.  At N = 1 this
+is the 8192^3 GEMM, at N = 8 the M = 65536 row-sharded GEMM.  A, B ~
+fp16(N(0,1)/sqrt(8192)), C ~ N(0,1), seeded, generated on the device.  B is
+replicated once before timing by a peer copy over NVLink from rank 0's memory
+(CUDA IPC), timed separately; no collective runs on the data path.  Inputs
+(A 128 MiB, B 128 MiB, C 256 MiB per GPU) exceed the 126 MB L2, so no flush
+is needed between steps.
+
+One step = one launch of the tcgen05 GEMM over the GPU's shard.  `value` is
+the aggregate TFLOP/s over all ranks (2 M N K per step / the max over ranks of
+the device-timed step).  `e2e` times the same step through the C ABI with
+host buffers: pinned host -> device copies of A, B, C, the launch, and the
+device -> host copy of C, all inside the timed region.  The line also
+carries VecAdd (n = 2^28 fp32 per GPU, HBM-bound) and the decode-shaped GEMM
+(M=16, N=14336, K=4096) as secondary results, each against its roofline.
+
+`--impl reference` times the reference's CPU implementation of the path (the
+i-j-k float32 loop of its tests, restated in C under oracle/) on all host
+threads, on a bounded sample of rows of the same workload; under torchrun
+only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "cuda-ir.go_b200"))
+
+METRIC = "fp16 GEMM TFLOP/s & % tensor peak; VecAdd GB/s & % HBM; at 1/2/4/8 GPUs"
+ROWS_PER_GPU = 8192
+N_DIM = 8192
+K_DIM = 8192
+VEC_N = 1 << 28
+SKINNY = (16, 14336, 4096)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic():
+    """DRAM bytes per launch from the committed ncu summaries
+    (profiles/dram_traffic.txt: `<workload> <bytes>` lines)."""
+    out = {}
+    p = os.path.join(REPO, "profiles", "dram_traffic.txt")
+    if os.path.exists(p):
+        for line in open(p):
+            parts = line.split()
+            if len(parts) >= 2 and not line.startswith("#"):
+                try:
+                    out[parts[0]] = float(parts[1])
+                except ValueError:
+                    pass
+    return out
+
+
+# ---- clocks during the timed region ------------------------------------------
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU through NVML in a
+    background thread (read-only queries)."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int, period_s: float = 0.002):
+        self.index, self.period = index, period_s
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            uuid_env = os.environ.get("CUDA_VISIBLE_DEVICES")
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self._physical_index(index, uuid_env))
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: report no clocks rather than guess
+            log(f"clock sampler unavailable: {e}")
+
+    @staticmethod
+    def _physical_index(index, env):
+        if env:
+            ids = [x for x in env.split(",") if x.strip()]
+            if index < len(ids) and ids[index].strip().isdigit():
+                return int(ids[index])
+        return index
+
+    def _sample(self):
+        nv = self._nv
+        mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+        try:
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        except Exception:
+            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+        self.samples.append(mhz)
+        for name, bit in self.REASONS.items():
+            if r & bit:
+                self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+            try:
+                self._sample()
+            except Exception:
+                pass
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+# ---- distributed plumbing -------------------------------------------------------
+
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return world, rank, local  # CPU only: no process group, no GPU
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---- timing helpers ----------------------------------------------------------------
+
+
+def time_steps(fn, steps, warmup, world, dev, sampler=None):
+    """W untimed warm-up steps, then K steps bracketed by barrier + synchronize,
+    timed with CUDA events on the current stream; returns ms per step (max
+    over ranks)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx = sampler if sampler is not None else _Null()
+    with ctx:
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(end) / steps
+    return max_over_ranks(ms, world, dev)
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+# ---- B replication by peer copy ------------------------------------------------
+
+
+def replicate_b(b, world, rank, dev):
+    """Copies rank 0's B into every other rank's local B over NVLink: rank 0
+    exports its allocation (CUDA IPC), the others map it, copy it into local
+    HBM with one device-to-device copy and unmap it.  Returns the max copy
+    time over ranks in ms."""
+    if world == 1:
+        return 0.0
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from cudair import _lib
+    L = _lib.lib()
+    handle = (ctypes.c_uint8 * 64)()
+    if rank == 0:
+        _lib.check(L.cudair_ipc_export(ctypes.c_void_p(b.data_ptr()), handle))
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(handle) if rank == 0 else None)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ms = 0.0
+    if rank != 0:
+        h = (ctypes.c_uint8 * 64).from_buffer_copy(handles[0])
+        peer = ctypes.c_void_p()
+        _lib.check(L.cudair_ipc_open(h, ctypes.byref(peer)))
+        s = torch.cuda.current_stream()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        _lib.check(L.cudair_peer_copy(ctypes.c_void_p(b.data_ptr()), peer, b.numel() * b.element_size(),
+                                      ctypes.c_void_p(s.cuda_stream)))
+        ev1.record()
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        _lib.check(L.cudair_ipc_close(peer))
+    dist.barrier()
+    log(f"rank {rank}: B replicated in {ms:.3f} ms (wall {1e3 * (time.perf_counter() - t0):.1f} ms)")
+    return max_over_ranks(ms, world, dev)
+
+
+# ---- CPU baseline (the reference's CPU loop, restated in C) ---------------------
+
+
+class CpuGemm:
+    """The reference's CPU loop for this path: the i-j-k float32 GEMM of its
+    tests (advanced_test.go:466-475, restated in oracle/oracle.c), over whole
+    rows of the 8192 x 8192 x 8192 problem; rows are independent, so a sample
+    of rows measures the loop's rate exactly."""
+
+    def __init__(self, max_rows: int):
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle
+        self.o = oracle
+        s = 1.0 / math.sqrt(K_DIM)
+        self.af = oracle.f16_to_f32(oracle.f32_to_f16(
+            oracle.normal(max_rows * K_DIM, 106, 0.0, s))).reshape(max_rows, K_DIM)
+        self.bf = oracle.f16_to_f32(oracle.f32_to_f16(
+            oracle.normal(K_DIM * N_DIM, 107, 0.0, s))).reshape(K_DIM, N_DIM)
+        self.c = oracle.normal(max_rows * N_DIM, 108).reshape(max_rows, N_DIM)
+
+    def run(self, rows: int, threads: int) -> float:
+        """Seconds to compute `rows` rows on `threads` threads."""
+        t0 = time.perf_counter()
+        self.o.gemm_ijk(self.af[:rows], self.bf, self.c[:rows], threads=threads)
+        return time.perf_counter() - t0
+
+    def sample(self, threads: int, budget_s: float):
+        """Rows sized to about budget_s seconds; returns (TFLOP/s, rows, s)."""
+        rows = threads
+        dt = self.run(rows, threads)
+        more = int(max(0.0, budget_s - dt) / max(dt / rows, 1e-9))
+        more = min(more, self.af.shape[0] - rows)
+        more -= more % max(1, threads)
+        if more > 0:
+            dt2 = self.run(more, threads)
+            rows, dt = rows + more, dt + dt2
+        return 2.0 * rows * N_DIM * K_DIM / dt / 1e12, rows, dt
+
+
+def run_reference(args, world, rank):
+    """The reference arm: the CPU i-j-k loop on all host threads, rank 0 only;
+    each step computes one row per thread of the workload."""
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    threads = oracle.num_threads()
+    cpu = CpuGemm(max_rows=threads)
+    rows_total, secs_total = 0, 0.0
+    for i in range(args.warmup + args.steps):
+        dt = cpu.run(threads, threads)
+        if i >= args.warmup:
+            rows_total += threads
+            secs_total += dt
+    value = 2.0 * rows_total * N_DIM * K_DIM / secs_total / 1e12
+    sample = (f"{rows_total} rows of C = A.B + C with N=K={N_DIM} over {args.steps} steps "
+              f"({threads} rows per step, one per thread), i-j-k float32 loop")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * secs_total / max(1, args.steps), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16-rounded inputs)",
+        "data": "synthetic (seeded N(0,1)/sqrt(K) operands)",
+        "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(n_gpus):
+    return {"workload": "row-sharded MatMul16 GEMM C=A.B+C (fp16 A,B; fp32 C, fp32 accumulate)",
+            "M": ROWS_PER_GPU * n_gpus, "N": N_DIM, "K": K_DIM, "rows_per_gpu": ROWS_PER_GPU,
+            "partition": "row blocks of A and C; B replicated by peer copy",
+            "l2": "inputs exceed L2 (512 MiB per GPU vs 126 MB)",
+            "secondary": {"vecadd_n_per_gpu": VEC_N, "skinny_MNK": list(SKINNY)}}
+
+
+# ---- our arm -------------------------------------------------------------------------
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    from cudair import kernels
+
+    dev = torch.device("cuda", local)
+    peaks, peak_kind = load_peaks()
+    traffic = load_traffic()
+    g = torch.Generator(device=dev)
+
+    # -- inputs in HBM
+    M, N, K = ROWS_PER_GPU, N_DIM, K_DIM
+    g.manual_seed(6000 + rank)
+    a = (torch.randn(M, K, generator=g, device=dev) / math.sqrt(K)).half()
+    b = torch.empty(K, N, dtype=torch.float16, device=dev)
+    if rank == 0:
+        g.manual_seed(7000)
+        b.copy_((torch.randn(K, N, generator=g, device=dev) / math.sqrt(K)).half())
+    g.manual_seed(8000 + rank)
+    c = torch.randn(M, N, generator=g, device=dev)
+    torch.cuda.synchronize()
+    b_ms = replicate_b(b, world, rank, dev)
+
+    flops = 2.0 * M * N * K
+    sampler = ClockSampler(local)
+    step = lambda: kernels.gemm(a, b, c)  # noqa: E731
+    ms = time_steps(step, args.steps, args.warmup, world, dev, sampler)
+    clocks = sampler.summary()
+    kernels.wait_status(clear=True)
+    value = flops * world / (ms * 1e-3) / 1e12
+    per_gpu = flops / (ms * 1e-3) / 1e12
+    log(f"rank {rank}: gemm {ms:.4f} ms/step, {per_gpu:.1f} TFLOP/s per GPU")
+
+    # -- e2e: host buffers, copies inside the timed region
+    a_h = a.cpu().pin_memory()
+    b_h = b.cpu().pin_memory()
+    c_h = c.cpu().pin_memory()
+    c_out = torch.empty_like(c_h).pin_memory()
+    a_d, b_d, c_d = torch.empty_like(a), torch.empty_like(b), torch.empty_like(c)
+
+    def e2e_step():
+        a_d.copy_(a_h, non_blocking=True)
+        b_d.copy_(b_h, non_blocking=True)
+        c_d.copy_(c_h, non_blocking=True)
+        kernels.gemm(a_d, b_d, c_d)
+        c_out.copy_(c_d, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    e2e_ms = time_steps(e2e_step, e2e_steps, max(3, min(args.warmup, 3)), world, dev)
+    e2e_value = flops * world / (e2e_ms * 1e-3) / 1e12
+    h2d = a_h.numel() * 2 + b_h.numel() * 2 + c_h.numel() * 4
+    d2h = c_out.numel() * 4
+    del a_h, b_h, c_h, c_out, a_d, b_d, c_d
+
+    # -- optional all-gather of C (reassembly; not part of the step)
+    gather = None
+    if args.gather and world > 1:
+        import torch.distributed as dist
+        full = torch.empty(world * M, N, dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(full, c)
+        torch.cuda.synchronize()
+        t = time_steps(lambda: dist.all_gather_into_tensor(full, c), 3, 1, world, dev)
+        gather = {"ms": t, "bytes_received_per_gpu": (world - 1) * M * N * 4,
+                  "GB/s_per_gpu": (world - 1) * M * N * 4 / (t * 1e-3) / 1e9}
+        del full
+
+    # -- secondary: VecAdd 2^28 per GPU
+    torch.cuda.empty_cache()
+    g.manual_seed(4000 + rank)
+    va = torch.rand(VEC_N, generator=g, device=dev) * 2 - 1
+    vb = torch.rand(VEC_N, generator=g, device=dev) * 2 - 1
+    vo = torch.empty_like(va)
+    v_ms = time_steps(lambda: kernels.vecadd(va, vb, vo), args.steps, args.warmup, world, dev)
+    v_bytes = 3 * 4 * VEC_N
+    v_gbs = v_bytes / (v_ms * 1e-3) / 1e9
+    del va, vb, vo
+
+    # -- secondary: decode-shaped GEMM (memory-bound on B)
+    sm, sn, sk = SKINNY
+    g.manual_seed(9000 + rank)
+    sa = torch.randn(sm, sk, generator=g, device=dev).half()
+    sb = (torch.randn(sk, sn, generator=g, device=dev) * 0.02).half()
+    sc = torch.zeros(sm, sn, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MiB > L2
+
+    def skinny_step():
+        flush.zero_()  # evicts B from L2 so each step streams it from HBM
+        kernels.gemm(sa, sb, sc)
+
+    # time the GEMM alone with events around it, flushing between steps
+    for _ in range(args.warmup):
+        skinny_step()
+    torch.cuda.synchronize()
+    s_times = []
+    for _ in range(max(5, min(args.steps, 50))):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        kernels.gemm(sa, sb, sc)
+        e1.record()
+        torch.cuda.synchronize()
+        s_times.append(e0.elapsed_time(e1))
+    s_ms = max_over_ranks(statistics.mean(s_times), world, dev)
+    s_bytes = sk * sn * 2 + sm * sk * 2 + 2 * sm * sn * 4
+    s_gbs = s_bytes / (s_ms * 1e-3) / 1e9
+    del sa, sb, sc, flush
+    kernels.wait_status(clear=True)
+
+    # -- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        r, rows, dt = CpuGemm(max_rows=256).sample(1, budget_s=args.cpu_budget)
+        cpu = {"value": r, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+               "sample": f"{rows} rows of the 8192^3 C = A.B + C by the i-j-k float32 loop "
+                         f"(oracle/oracle.c restating advanced_test.go:466-475), 1 thread, "
+                         f"{dt:.1f} s"}
+
+    if rank != 0:
+        return
+    tensor_peak = peaks["bf16_tflops"]
+    achieved = flops / (ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1)/sqrt(8192) fp16 operands, N(0,1) fp32 C)",
+        "config": workload_config(world),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tensor_peak,
+                     "unit": "TFLOP/s", "frac": achieved / tensor_peak,
+                     "traffic": traffic.get("gemm_8192"),
+                     "peak_kind": f"{peak_kind} bf16 burst (fp16 dense rate is equal)",
+                     "frac_of_nominal": achieved / 2250.0},
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "cpu_baseline": cpu,
+        "gpu_launches": args.steps * world,
+        "clocks": clocks,
+        "b_replication_ms": b_ms,
+        "gather": gather,
+        "vecadd": {"value": v_gbs * world, "unit": "GB/s", "ms_per_step": v_ms, "n_per_gpu": VEC_N,
+                   "roofline": {"bound": "hbm", "achieved": v_gbs, "peak": peaks["hbm_gbs"],
+                                "unit": "GB/s", "frac": v_gbs / peaks["hbm_gbs"],
+                                "traffic": traffic.get("vecadd_2p28"),
+                                "frac_of_nominal": v_gbs / 8000.0}},
+        "skinny": {"M": sm, "N": sn, "K": sk, "ms": s_ms, "GB/s": s_gbs,
+                   "TFLOP/s": 2.0 * sm * sn * sk / (s_ms * 1e-3) / 1e12,
+                   "roofline": {"bound": "hbm", "achieved": s_gbs, "peak": peaks["hbm_gbs"],
+                                "unit": "GB/s", "frac": s_gbs / peaks["hbm_gbs"],
+                                "traffic": traffic.get("skinny_16x14336x4096")}},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--gather", action="store_true", help="also all-gather C over NCCL (timed apart)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds for the CPU baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            if dist.is_initialized():
+                dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,92 @@
+// launchers.cu - the module kernels (module_kernels.cuh) compiled into the
+// library, the C-ABI launchers for VecAdd and ReduceF32, and the B
+// replication primitives of the row-sharded multi-GPU GEMM.
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include "cudair_internal.h"
+#include "module_kernels.cuh"
+
+using namespace cudair;
+
+// VecAdd on a persistent grid: 4 CTAs of 512 threads per SM (every SM kept
+// at full occupancy, 16 loads of 16 bytes in flight per thread pair), capped
+// by the work so small n does not launch idle CTAs.
+CUDAIR_API int cudair_vecadd(const float *a, const float *b, float *out, int32_t n, void *stream) {
+    clear_error();
+    if (n < 0) return set_error(CUDAIR_ERR_INVALID, "cudair: VecAdd: n = %d", n);
+    if (n == 0) return CUDAIR_OK;
+    if (!a || !b || !out) return set_error(CUDAIR_ERR_INVALID, "cudair: VecAdd: nil pointer");
+    int sms = 0;
+    int rc = sm_count_current_device(&sms);
+    if (rc != CUDAIR_OK) return rc;
+    constexpr int kThreads = 512;
+    const int64_t vec_work = (static_cast<int64_t>(n) + 3) / 4;
+    int64_t blocks = (vec_work + kThreads - 1) / kThreads;
+    const int64_t cap = static_cast<int64_t>(sms) * 4;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    VecAdd<<<static_cast<unsigned>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, b, out, n);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "VecAdd launch");
+    return CUDAIR_OK;
+}
+
+CUDAIR_API int cudair_reduce_f32(const float *in, float *out, int32_t n, void *stream) {
+    clear_error();
+    if (n < 0 || n % 32 != 0)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: ReduceF32: n = %d, want a multiple of 32", n);
+    if (n == 0) return CUDAIR_OK;
+    if (!in || !out) return set_error(CUDAIR_ERR_INVALID, "cudair: ReduceF32: nil pointer");
+    int sms = 0;
+    int rc = sm_count_current_device(&sms);
+    if (rc != CUDAIR_OK) return rc;
+    // The kernel reads one element per launched thread, so the launch covers
+    // exactly n threads: 256-thread blocks when they divide n, else warps.
+    const int threads = (n % 256 == 0) ? 256 : 32;
+    ReduceF32<<<n / threads, threads, 0, static_cast<cudaStream_t>(stream)>>>(in, out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "ReduceF32 launch");
+    return CUDAIR_OK;
+}
+
+// ---- B replication for the row-sharded GEMM -----------------------------------
+
+CUDAIR_API int cudair_ipc_export(const void *dev_ptr, void *handle_out) {
+    clear_error();
+    if (!dev_ptr || !handle_out) return set_error(CUDAIR_ERR_INVALID, "cudair: ipc_export: nil pointer");
+    static_assert(sizeof(cudaIpcMemHandle_t) == CUDAIR_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr));
+    if (e != cudaSuccess) return cuda_error(e, "cudaIpcGetMemHandle");
+    memcpy(handle_out, &h, sizeof(h));
+    return CUDAIR_OK;
+}
+
+CUDAIR_API int cudair_ipc_open(const void *handle, void **dev_ptr_out) {
+    clear_error();
+    if (!handle || !dev_ptr_out) return set_error(CUDAIR_ERR_INVALID, "cudair: ipc_open: nil pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_error(e, "cudaIpcOpenMemHandle");
+    return CUDAIR_OK;
+}
+
+CUDAIR_API int cudair_ipc_close(void *dev_ptr) {
+    clear_error();
+    if (!dev_ptr) return CUDAIR_OK;
+    cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    if (e != cudaSuccess) return cuda_error(e, "cudaIpcCloseMemHandle");
+    return CUDAIR_OK;
+}
+
+CUDAIR_API int cudair_peer_copy(void *dst, const void *src, size_t bytes, void *stream) {
+    clear_error();
+    if (bytes == 0) return CUDAIR_OK;
+    if (!dst || !src) return set_error(CUDAIR_ERR_INVALID, "cudair: peer_copy: nil pointer");
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice,
+                                    static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyAsync(peer)");
+    return CUDAIR_OK;
+}

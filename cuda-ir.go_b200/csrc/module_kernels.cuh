@@ -1,0 +1,196 @@
+// module_kernels.cuh - the kernels that keep the reference's entry-point
+// names and parameter ABI (one 8-byte pointer per cuda.Buf[T], int32 n), so a
+// caller that loads the module and launches them by name with the reference's
+// own launch configurations gets the same results.
+//
+// Compiled twice: into cudair_kernels.cubin (the loadable module that stands
+// in for the PTX the reference's compiler emits) and into libcudair_b200.so
+// (behind the C-ABI launchers).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+// ---- VecAdd -----------------------------------------------------------------
+
+// out[i] = a[i] + b[i] for i < n.  examples/vecadd/vecadd.go:6-11.
+//
+// The reference gives each thread one scalar element (launched
+// LaunchConfig1D(n, 256), main_test.go:37).  Here every thread walks a
+// grid-stride loop over 16-byte vectors, four vectors per trip with all loads
+// issued before the adds, so the same entry is correct under that launch (most
+// threads then find no work) and saturates HBM under a persistent launch of a
+// few CTAs per SM.  Loads and stores use the streaming (evict-first) cache
+// policy: every byte is touched once.  When the three pointers do not share
+// their offset within 16 bytes the loop falls back to scalar accesses.  The
+// add is IEEE round-to-nearest, bit-exact with the CPU's float32 add.
+extern "C" __global__ void __launch_bounds__(1024)
+    VecAdd(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ out,
+           int n) {
+    if (n <= 0) return;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const uintptr_t mis = reinterpret_cast<uintptr_t>(out) & 15u;
+    if ((reinterpret_cast<uintptr_t>(a) & 15u) == mis &&
+        (reinterpret_cast<uintptr_t>(b) & 15u) == mis && (mis & 3u) == 0) {
+        int64_t head = static_cast<int64_t>((16u - mis) & 15u) >> 2;  // scalars before 16B
+        if (head > n) head = n;
+        if (tid < head) out[tid] = __fadd_rn(a[tid], b[tid]);
+        const int64_t n4 = (n - head) >> 2;
+        const float4 *a4 = reinterpret_cast<const float4 *>(a + head);
+        const float4 *b4 = reinterpret_cast<const float4 *>(b + head);
+        float4 *o4 = reinterpret_cast<float4 *>(out + head);
+        constexpr int U = 4;
+        int64_t i = tid;
+        for (; i + (U - 1) * nthr < n4; i += U * nthr) {
+            float4 va[U], vb[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                va[u] = __ldcs(a4 + i + u * nthr);
+                vb[u] = __ldcs(b4 + i + u * nthr);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float4 r;
+                r.x = __fadd_rn(va[u].x, vb[u].x);
+                r.y = __fadd_rn(va[u].y, vb[u].y);
+                r.z = __fadd_rn(va[u].z, vb[u].z);
+                r.w = __fadd_rn(va[u].w, vb[u].w);
+                __stcs(o4 + i + u * nthr, r);
+            }
+        }
+        for (; i < n4; i += nthr) {
+            const float4 va = __ldcs(a4 + i), vb = __ldcs(b4 + i);
+            float4 r;
+            r.x = __fadd_rn(va.x, vb.x);
+            r.y = __fadd_rn(va.y, vb.y);
+            r.z = __fadd_rn(va.z, vb.z);
+            r.w = __fadd_rn(va.w, vb.w);
+            __stcs(o4 + i, r);
+        }
+        const int64_t t = head + 4 * n4 + tid;  // at most 3 trailing scalars
+        if (t < n) out[t] = __fadd_rn(a[t], b[t]);
+    } else {
+        for (int64_t i = tid; i < n; i += nthr) out[i] = __fadd_rn(a[i], b[i]);
+    }
+}
+
+// ---- MatMul16 ---------------------------------------------------------------
+
+namespace cudair_detail {
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *p) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+
+// D = A(16x16, row) . B(16x8, col) + D, fp16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+}  // namespace cudair_detail
+
+// C = A.B + C for n x n row-major matrices (fp16 A, B; fp32 C in place),
+// examples/hopper/hopper.go:201-226, under the reference's launch contract:
+// grid (n/16, n/16), one 32-thread block per 16x16 tile of C
+// (advanced_test.go:477).  n must be a multiple of 16, as there.
+//
+// This entry serves callers that launch the module kernel themselves with
+// that geometry; the throughput path is the tcgen05 kernel behind
+// cudair_matmul16(), which needs tensor-map parameters this signature cannot
+// carry.  The warp keeps its C tile in mma.sync accumulators initialised from
+// C, streams 16-wide k-slices of A and B through padded shared memory
+// (conflict-free ldmatrix rows) with the next slice's global loads in flight
+// during the current slice's two m16n8k16 MMAs, and writes C back once.
+// Threads beyond the first warp return.
+extern "C" __global__ void __launch_bounds__(32)
+    MatMul16(const __half *__restrict__ a, const __half *__restrict__ b, float *__restrict__ c,
+             int n) {
+    using namespace cudair_detail;
+    if (threadIdx.x >= 32 || threadIdx.y != 0 || threadIdx.z != 0) return;
+    const int row0 = blockIdx.y * 16, col0 = blockIdx.x * 16;
+    if (n <= 0 || (n & 15) != 0 || row0 >= n || col0 >= n) return;
+
+    __shared__ __align__(16) __half sa[16][24];  // 48-byte rows
+    __shared__ __align__(16) __half sb[16][24];
+
+    const int lane = threadIdx.x, g = lane >> 2, t = lane & 3;
+    const size_t N = static_cast<size_t>(n);
+
+    float acc[2][4];
+#pragma unroll
+    for (int nf = 0; nf < 2; ++nf) {
+        const float2 lo = *reinterpret_cast<const float2 *>(c + (row0 + g) * N + col0 + nf * 8 + 2 * t);
+        const float2 hi =
+            *reinterpret_cast<const float2 *>(c + (row0 + g + 8) * N + col0 + nf * 8 + 2 * t);
+        acc[nf][0] = lo.x;
+        acc[nf][1] = lo.y;
+        acc[nf][2] = hi.x;
+        acc[nf][3] = hi.y;
+    }
+
+    // Lane l stages 8 halves of row l/2 of the A slice and of the B slice.
+    const int sr = lane >> 1, sc = (lane & 1) * 8;
+    const __half *ap = a + (row0 + sr) * N + sc;
+    const __half *bp = b + sr * N + col0 + sc;
+    uint4 ra = *reinterpret_cast<const uint4 *>(ap);
+    uint4 rb = *reinterpret_cast<const uint4 *>(bp);
+
+    for (int k0 = 0; k0 < n; k0 += 16) {
+        *reinterpret_cast<uint4 *>(&sa[sr][sc]) = ra;
+        *reinterpret_cast<uint4 *>(&sb[sr][sc]) = rb;
+        __syncwarp();
+        if (k0 + 16 < n) {
+            ra = *reinterpret_cast<const uint4 *>(ap + k0 + 16);
+            rb = *reinterpret_cast<const uint4 *>(bp + (k0 + 16) * N);
+        }
+        uint32_t fa[4], fb[4];
+        ldsm_x4(fa, &sa[lane & 15][(lane >> 4) * 8]);
+        ldsm_x4_trans(fb, &sb[lane & 15][(lane >> 4) * 8]);
+        mma_16816(acc[0], fa, fb[0], fb[1]);
+        mma_16816(acc[1], fa, fb[2], fb[3]);
+        __syncwarp();
+    }
+
+#pragma unroll
+    for (int nf = 0; nf < 2; ++nf) {
+        *reinterpret_cast<float2 *>(c + (row0 + g) * N + col0 + nf * 8 + 2 * t) =
+            make_float2(acc[nf][0], acc[nf][1]);
+        *reinterpret_cast<float2 *>(c + (row0 + g + 8) * N + col0 + nf * 8 + 2 * t) =
+            make_float2(acc[nf][2], acc[nf][3]);
+    }
+}
+
+// ---- ReduceF32 ----------------------------------------------------------------
+
+// out[2w] = min, out[2w+1] = max of the 32 values of warp w,
+// examples/blackwell/blackwell.go:8-17, with Blackwell's float warp
+// reductions (redux.sync.{min,max}.f32, sm_100a).  The .NaN form propagates a
+// NaN, like Go's math.Min/Max in the reference's check.  Like the reference,
+// every launched thread reads one element: the launch covers exactly n.
+extern "C" __global__ void ReduceF32(const float *__restrict__ in, float *__restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const float v = in[i];
+    float mn, mx;
+    asm volatile("redux.sync.min.NaN.f32 %0, %1, 0xffffffff;" : "=f"(mn) : "f"(v));
+    asm volatile("redux.sync.max.NaN.f32 %0, %1, 0xffffffff;" : "=f"(mx) : "f"(v));
+    if ((threadIdx.x & 31) == 0) {
+        out[2 * (i / 32)] = mn;
+        out[2 * (i / 32) + 1] = mx;
+    }
+}

@@ -1,0 +1,93 @@
+"""Launchers of the tuned sm_100a kernels over the C ABI, taking torch CUDA
+tensors (device memory and streams come from torch; the arithmetic is the
+library's).  Each call is asynchronous on the given stream (default: torch's
+current stream).
+"""
+from __future__ import annotations
+
+import ctypes
+
+from ._lib import CudairError, check, lib
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def _need(t, dtype, name):
+    import torch
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise CudairError(1, f"cudair: {name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise CudairError(1, f"cudair: {name} must be {dtype}, got {t.dtype}")
+
+
+def matmul16(a, b, c, stream=None) -> None:
+    """c += a @ b for n x n row-major fp16 a, b and fp32 c (MatMul16's operands)."""
+    import torch
+    _need(a, torch.float16, "a")
+    _need(b, torch.float16, "b")
+    _need(c, torch.float32, "c")
+    n = a.shape[0]
+    if not (a.shape == b.shape == c.shape == (n, n)) or not (
+            a.is_contiguous() and b.is_contiguous() and c.is_contiguous()):
+        raise CudairError(1, "cudair: MatMul16: a, b, c must be contiguous n x n")
+    check(lib().cudair_matmul16(a.data_ptr(), b.data_ptr(), c.data_ptr(), n, _stream(stream)))
+
+
+def gemm(a, b, c, stream=None) -> None:
+    """c += a @ b: a (M x K) and b (K x N) fp16, c (M x N) fp32, row-major with
+    unit inner stride."""
+    import torch
+    _need(a, torch.float16, "a")
+    _need(b, torch.float16, "b")
+    _need(c, torch.float32, "c")
+    M, K = a.shape
+    K2, N = b.shape
+    if K2 != K or tuple(c.shape) != (M, N):
+        raise CudairError(1, f"cudair: gemm: shapes {tuple(a.shape)} {tuple(b.shape)} {tuple(c.shape)}")
+    for t, nm in ((a, "a"), (b, "b"), (c, "c")):
+        if t.stride(1) != 1:
+            raise CudairError(1, f"cudair: gemm: {nm} needs unit inner stride")
+    check(lib().cudair_gemm_f16f32(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K,
+                                   a.stride(0), b.stride(0), c.stride(0), _stream(stream)))
+
+
+def vecadd(a, b, out, stream=None) -> None:
+    """out = a + b over fp32 vectors (VecAdd's operands)."""
+    import torch
+    for t, nm in ((a, "a"), (b, "b"), (out, "out")):
+        _need(t, torch.float32, nm)
+    n = out.numel()
+    if a.numel() != n or b.numel() != n:
+        raise CudairError(1, "cudair: VecAdd: length mismatch")
+    check(lib().cudair_vecadd(a.data_ptr(), b.data_ptr(), out.data_ptr(), n, _stream(stream)))
+
+
+def reduce_f32(x, out, stream=None) -> None:
+    """out[2w], out[2w+1] = min, max of warp w's 32 values (ReduceF32)."""
+    import torch
+    _need(x, torch.float32, "in")
+    _need(out, torch.float32, "out")
+    check(lib().cudair_reduce_f32(x.data_ptr(), out.data_ptr(), x.numel(), _stream(stream)))
+
+
+def wait_status(clear: bool = True) -> int:
+    """Synchronises and returns the bounded-wait status word (0 = no wait gave
+    up); raises CudairError(ERR_TIMEOUT) when a bit is set."""
+    v = ctypes.c_uint32()
+    rc = lib().cudair_wait_status(ctypes.byref(v), 1 if clear else 0)
+    if rc != 0:
+        err = CudairError(rc, lib().cudair_last_error().decode())
+        err.status = v.value
+        raise err
+    return v.value
+
+
+def wait_timeout_selftest(limit_ns: int, stream=None) -> None:
+    check(lib().cudair_wait_timeout_selftest(limit_ns, _stream(stream)))

@@ -1,0 +1,207 @@
+/*
+ * cudair_b200.h - the C ABI of the B200 (sm_100a) build of cuda-ir.go's
+ * MatMul16 / VecAdd path.
+ *
+ * Two things replace the reference's compiled kernels and host helpers:
+ *
+ *  1. A kernel module image (cudair_kernels.cubin, sm_100a) whose entry
+ *     points keep the reference's names and parameter ABI, so a caller that
+ *     loads a module and launches "MatMul16" / "VecAdd" / "ReduceF32" by name
+ *     (gocudrv ctx.LoadModule + Function.Launch) runs them unchanged:
+ *       MatMul16(const __half* a, const __half* b, float* c, int32 n)
+ *           examples/hopper/hopper.go:201 (launched as in advanced_test.go:477)
+ *       VecAdd(const float* a, const float* b, float* out, int32 n)
+ *           examples/vecadd/vecadd.go:6   (launched as in main_test.go:37)
+ *       ReduceF32(const float* in, float* out)
+ *           examples/blackwell/blackwell.go:8
+ *     Each cuda.Buf[T] parameter is one 8-byte device pointer and int32 is
+ *     4 bytes, the layout the reference's compiler gives them
+ *     (build.go:809-820).
+ *
+ *  2. This shared library (libcudair_b200.so): the reference's host/ helpers
+ *     (tensor maps, module loading, cuLaunchKernelEx launches) and launchers
+ *     for the tuned sm_100a kernels, all behind plain C types.
+ *
+ * Conventions: every function returns CUDAIR_OK (0) or an error code; the
+ * message of the calling thread's last error is cudair_last_error().  Device
+ * pointers are passed as plain pointers / uint64_t.  A NULL stream is the
+ * legacy default stream.  Calls use the CUDA context current on the calling
+ * thread, making the device's primary context current when there is none
+ * (the context gocudrv itself uses).  No function allocates device memory
+ * unless its comment says so; the caller owns every buffer.
+ */
+#ifndef CUDAIR_B200_H
+#define CUDAIR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- errors ------------------------------------------------------------ */
+
+enum {
+    CUDAIR_OK = 0,
+    CUDAIR_ERR_INVALID = 1,   /* argument validation failed (nothing launched) */
+    CUDAIR_ERR_DRIVER = 2,    /* libcuda could not be opened / a symbol is missing */
+    CUDAIR_ERR_CUDA = 3,      /* a CUDA driver or runtime call failed */
+    CUDAIR_ERR_TIMEOUT = 4,   /* a bounded device-side wait gave up (see cudair_wait_status) */
+    CUDAIR_ERR_UNSUPPORTED = 5 /* the device is not sm_100 */
+};
+
+/* Message of the calling thread's last failed call ("" if none).  Replaces
+ * the error values of host/driver.go:108-113 and the "host: EncodeTiled: ..."
+ * strings of host/tensormap.go:228-253, which it reproduces verbatim. */
+const char *cudair_last_error(void);
+
+/* Library version string. */
+const char *cudair_version(void);
+
+/* ---- tensor maps (host/tensormap.go) ----------------------------------- */
+
+/* Enum values are CUtensorMap*'s, as in host/tensormap.go:37-108. */
+enum {
+    CUDAIR_TENSOR_MAP_UINT8 = 0, CUDAIR_TENSOR_MAP_UINT16 = 1,
+    CUDAIR_TENSOR_MAP_UINT32 = 2, CUDAIR_TENSOR_MAP_INT32 = 3,
+    CUDAIR_TENSOR_MAP_UINT64 = 4, CUDAIR_TENSOR_MAP_INT64 = 5,
+    CUDAIR_TENSOR_MAP_FLOAT16 = 6, CUDAIR_TENSOR_MAP_FLOAT32 = 7,
+    CUDAIR_TENSOR_MAP_FLOAT64 = 8, CUDAIR_TENSOR_MAP_BFLOAT16 = 9,
+    CUDAIR_TENSOR_MAP_FLOAT32_FTZ = 10, CUDAIR_TENSOR_MAP_TFLOAT32 = 11,
+    CUDAIR_TENSOR_MAP_TFLOAT32_FTZ = 12
+};
+enum { CUDAIR_INTERLEAVE_NONE = 0, CUDAIR_INTERLEAVE_16B = 1, CUDAIR_INTERLEAVE_32B = 2 };
+enum { CUDAIR_SWIZZLE_NONE = 0, CUDAIR_SWIZZLE_32B = 1, CUDAIR_SWIZZLE_64B = 2, CUDAIR_SWIZZLE_128B = 3 };
+enum { CUDAIR_L2_PROMOTION_NONE = 0, CUDAIR_L2_PROMOTION_64B = 1,
+       CUDAIR_L2_PROMOTION_128B = 2, CUDAIR_L2_PROMOTION_256B = 3 };
+enum { CUDAIR_OOB_FILL_NONE = 0, CUDAIR_OOB_FILL_NAN = 1 };
+
+#define CUDAIR_TENSOR_MAP_BYTES 128
+
+/*
+ * Encodes a tiled TMA tensor map into out (128 bytes, 64-byte aligned).
+ * Replaces host.EncodeTiled / host.EncodeTiledPtr (host/tensormap.go:167-224)
+ * with the same validation and messages (validate, :228-253): rank 1..5,
+ * n_box_dim == rank, n_global_strides == rank-1, n_element_strides == rank
+ * when element_strides is non-NULL, a 16-byte aligned pointer, box entries
+ * 1..256 and strides that are multiples of 16.  buffer_elem_size is the
+ * element size of the buffer the pointer came from (EncodeTiled's check,
+ * :171-174), or 0 to skip that check (EncodeTiledPtr).  element_strides may
+ * be NULL (all 1).  The arrays are innermost dimension first.
+ * Validation runs before the driver is touched, so it also works on a host
+ * without a GPU.
+ */
+int cudair_encode_tiled(void *out, uint32_t data_type, uint32_t rank,
+                        uint64_t global_address,
+                        const uint64_t *global_dim,
+                        const uint64_t *global_strides, uint32_t n_global_strides,
+                        const uint32_t *box_dim, uint32_t n_box_dim,
+                        const uint32_t *element_strides, uint32_t n_element_strides,
+                        uint32_t interleave, uint32_t swizzle,
+                        uint32_t l2_promotion, uint32_t oob_fill,
+                        uint32_t buffer_elem_size);
+
+/* ---- modules and attribute launches (host/launchex.go) ----------------- */
+
+typedef struct cudair_module_s *cudair_module;
+typedef struct cudair_function_s *cudair_function;
+
+/* Loads a module image (cubin or NUL-terminated PTX) into the current
+ * context.  Replaces host.LoadModule (host/launchex.go:45-70). */
+int cudair_module_load(const void *image, size_t len, cudair_module *out);
+/* Replaces Module.Close (host/launchex.go:73-80). */
+int cudair_module_unload(cudair_module m);
+/* Replaces Module.Function (host/launchex.go:83-101). */
+int cudair_module_function(cudair_module m, const char *name, cudair_function *out);
+
+/*
+ * Launches f with cuLaunchKernelEx and the attributes of host.LaunchAttrs
+ * (host/launchex.go:105-120, ids of :144-148): cluster_dim (NULL or all-zero
+ * adds none), cooperative, programmatic stream serialisation.  params is the
+ * usual void** array of pointers to each parameter's bytes.  A NULL stream
+ * synchronises the context afterwards, as Function.LaunchEx does
+ * (host/launchex.go:175-219).
+ */
+int cudair_launch_ex(cudair_function f, const uint32_t grid[3],
+                     const uint32_t block[3], uint32_t shared_mem_bytes,
+                     void *stream, const uint32_t cluster_dim[3],
+                     int cooperative, int programmatic_stream_serialization,
+                     void **params);
+
+/* Synchronises the current context (gocudrv ctx.Synchronize). */
+int cudair_ctx_synchronize(void);
+
+/* ---- tuned launchers for the hot path ----------------------------------- */
+
+/*
+ * C = A.B + C for n x n row-major matrices: fp16 A and B, fp32 C updated in
+ * place, fp32 accumulation.  Same operands as MatMul16 (hopper.go:201); this
+ * launcher runs the sm_100a tcgen05/TMA kernel on a persistent grid instead
+ * of the reference's one-warp-per-16x16-tile launch.  n must be a multiple of
+ * 16 (the reference's own requirement) and the pointers 16-byte aligned.
+ * Asynchronous on stream.
+ */
+int cudair_matmul16(const void *a, const void *b, float *c, int32_t n, void *stream);
+
+/*
+ * General form of the same GEMM: C (M x N, row stride ldc) += A (M x K,
+ * row stride lda) . B (K x N, row stride ldb), strides in elements.  Needs
+ * lda, ldb multiples of 8 and ldc a multiple of 4 (16-byte rows), 16-byte
+ * aligned pointers.  M, N or K of 0 is a no-op.  Asynchronous on stream.
+ */
+int cudair_gemm_f16f32(const void *a, const void *b, float *c,
+                       int64_t M, int64_t N, int64_t K,
+                       int64_t lda, int64_t ldb, int64_t ldc, void *stream);
+
+/*
+ * out[i] = a[i] + b[i] for i < n (fp32, round-to-nearest: bit-exact with a
+ * CPU add).  Same operands as VecAdd (vecadd.go:6); the launcher sizes a
+ * persistent grid over the SMs.  Any alignment is accepted.  Asynchronous.
+ */
+int cudair_vecadd(const float *a, const float *b, float *out, int32_t n, void *stream);
+
+/*
+ * Per-warp min and max of n floats: out[2w], out[2w+1] for warp w
+ * (blackwell.go:8-17, redux.sync.{min,max}.f32).  n must be a multiple of 32.
+ */
+int cudair_reduce_f32(const float *in, float *out, int32_t n, void *stream);
+
+/* ---- failure detection ----------------------------------------------------- */
+
+/*
+ * Every mbarrier wait inside the library's pipelined kernels is bounded.  A
+ * wait that gives up sets a bit in a device status word (which site gave up)
+ * and the kernel unwinds without trapping.  cudair_wait_status synchronises
+ * the current device, reads the word into *status (0 = no timeout) and, if
+ * clear != 0, zeroes it.  It returns CUDAIR_ERR_TIMEOUT when a bit was set.
+ */
+int cudair_wait_status(uint32_t *status, int clear);
+
+/*
+ * Self-test of the bounded wait: launches one CTA that waits on an mbarrier
+ * no one arrives on, with a limit of limit_ns nanoseconds.  The kernel gives
+ * up, records the timeout and returns, so the context stays usable.
+ */
+int cudair_wait_timeout_selftest(uint64_t limit_ns, void *stream);
+
+/* ---- multi-GPU: B replication by peer copy ----------------------------- */
+
+#define CUDAIR_IPC_HANDLE_BYTES 64
+
+/* Exports a device allocation for other processes (cudaIpcGetMemHandle). */
+int cudair_ipc_export(const void *dev_ptr, void *handle_out);
+/* Maps another process's allocation into this one (cudaIpcOpenMemHandle). */
+int cudair_ipc_open(const void *handle, void **dev_ptr_out);
+/* Unmaps it (cudaIpcCloseMemHandle). */
+int cudair_ipc_close(void *dev_ptr);
+/* Copies bytes from a peer GPU's memory into local memory over NVLink
+ * (cudaMemcpyAsync device-to-device on stream).  No kernel ever reads peer
+ * memory; the peer copy lands in local HBM first. */
+int cudair_peer_copy(void *dst, const void *src, size_t bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUDAIR_B200_H */

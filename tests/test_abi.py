@@ -1,0 +1,132 @@
+"""The C-ABI library on CPU: it loads, exports every function the header
+declares, and rejects bad arguments with the reference's messages before it
+touches the driver (TestTensorMap/Encode, hostapi_test.go:503-535, is the
+model for the tensor-map cases)."""
+import ctypes
+
+import pytest
+
+
+def test_library_exports_every_header_function(cudair):
+    from cudair import _lib
+    names = _lib.header_functions()
+    assert len(names) >= 18
+    for n in names:
+        assert hasattr(cudair.lib(), n), f"{n} declared in include/cudair_b200.h but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_module_image_has_reference_entry_points(cudair):
+    from cudair import host
+    img = host.KernelsImage()
+    assert img[:4] == b"\x7fELF"
+    for name in (b"MatMul16", b"VecAdd", b"ReduceF32"):
+        assert name + b"\x00" in img, name
+
+
+BASE = dict(GlobalDim=[64, 64], GlobalStrides=[64 * 4], BoxDim=[32, 32])
+PTR = 0x7F0000000000  # a 16-byte aligned address; never dereferenced on CPU
+
+
+def _encode(cudair, ptr=PTR, elem=4, **over):
+    from cudair import host
+    d = host.TiledTensor(DataType=host.TensorMapFloat32, **{**BASE, **over})
+    return host.EncodeTiledPtr(ptr, d, _elem_size=elem)
+
+
+@pytest.mark.parametrize("mutate,message", [
+    (dict(GlobalStrides=[64 * 4 + 4]), "host: EncodeTiled: GlobalStrides[0] = 260, want a multiple of 16"),
+    (dict(BoxDim=[512, 32]), "host: EncodeTiled: BoxDim[0] = 512, want 1..256"),
+    (dict(GlobalStrides=[256, 256]), "host: EncodeTiled: 2 GlobalStrides for rank 2, want 1"),
+    (dict(BoxDim=[32]), "host: EncodeTiled: 1 BoxDim for rank 2"),
+    (dict(GlobalDim=[1] * 6, GlobalStrides=[16] * 5, BoxDim=[1] * 6), "host: EncodeTiled: rank 6, want 1..5"),
+    (dict(ElementStrides=[1]), "host: EncodeTiled: 1 ElementStrides for rank 2"),
+])
+def test_encode_tiled_rejects_bad_descriptors(cudair, mutate, message):
+    with pytest.raises(cudair.CudairError) as e:
+        _encode(cudair, **mutate)
+    assert e.value.code == 1
+    assert str(e.value) == message
+
+
+def test_encode_tiled_rejects_element_size_mismatch(cudair):
+    from cudair import host
+    d = host.TiledTensor(DataType=host.TensorMapFloat16, **BASE)
+    with pytest.raises(cudair.CudairError) as e:
+        host.EncodeTiledPtr(PTR, d, _elem_size=4)
+    assert str(e.value) == "host: EncodeTiled: buffer element is 4 bytes, DataType is 2"
+
+
+def test_encode_tiled_rejects_unaligned_pointer(cudair):
+    with pytest.raises(cudair.CudairError) as e:
+        _encode(cudair, ptr=PTR + 4)
+    assert "is not 16-byte aligned" in str(e.value)
+
+
+def test_encode_tiled_rejects_nil_buffer(cudair):
+    with pytest.raises(cudair.CudairError) as e:
+        _encode(cudair, ptr=0)
+    assert str(e.value) == "host: EncodeTiled: nil buffer"
+
+
+def test_launch_ex_rejects_nil_function_and_empty_config(cudair):
+    grid = (ctypes.c_uint32 * 3)(1, 1, 1)
+    block = (ctypes.c_uint32 * 3)(32, 1, 1)
+    rc = cudair.lib().cudair_launch_ex(None, grid, block, 0, None, None, 0, 0, None)
+    assert rc == 1 and cudair.last_error() == "host: LaunchEx: nil function"
+
+
+def test_module_load_rejects_empty_image(cudair):
+    m = ctypes.c_void_p()
+    rc = cudair.lib().cudair_module_load(None, 0, ctypes.byref(m))
+    assert rc == 1 and cudair.last_error() == "host: LoadModule: empty PTX"
+
+
+def test_matmul16_rejects_n_not_multiple_of_16(cudair):
+    rc = cudair.lib().cudair_matmul16(16, 16, 16, 24, None)
+    assert rc == 1 and "multiple of 16" in cudair.last_error()
+
+
+def test_matmul16_zero_is_noop(cudair):
+    assert cudair.lib().cudair_matmul16(None, None, None, 0, None) == 0
+
+
+@pytest.mark.parametrize("args,needle", [
+    ((16, 16, 16, -1, 8, 8, 8, 8, 8), "negative size"),
+    ((16, 16, 16, 8, 8, 8, 4, 8, 8), "leading dimensions"),
+    ((16, 16, 16, 8, 8, 12, 12, 8, 8), "multiples of 8"),
+    ((24, 16, 16, 8, 8, 8, 8, 8, 8), "16-byte aligned"),
+    ((None, 16, 16, 8, 8, 8, 8, 8, 8), "nil pointer"),
+])
+def test_gemm_validation(cudair, args, needle):
+    rc = cudair.lib().cudair_gemm_f16f32(*args, None)
+    assert rc == 1 and needle in cudair.last_error(), cudair.last_error()
+
+
+def test_gemm_empty_sizes_are_noops(cudair):
+    for M, N, K in ((0, 8, 8), (8, 0, 8), (8, 8, 0)):
+        assert cudair.lib().cudair_gemm_f16f32(None, None, None, M, N, K, 8, 8, 8, None) == 0
+
+
+def test_vecadd_and_reduce_validation(cudair):
+    L = cudair.lib()
+    assert L.cudair_vecadd(None, None, None, -1, None) == 1
+    assert L.cudair_vecadd(None, None, None, 0, None) == 0
+    assert L.cudair_reduce_f32(16, 16, 33, None) == 1
+    assert "multiple of 32" in cudair.last_error()
+
+
+def test_errors_are_thread_local(cudair):
+    import threading
+    L = cudair.lib()
+    L.cudair_vecadd(None, None, None, -1, None)
+    seen = []
+
+    def other():
+        seen.append(cudair.last_error())
+
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    assert seen == [""]
+    assert "VecAdd" in cudair.last_error()

@@ -1,0 +1,229 @@
+"""MatMul16 on the B200: C = A.B + C with fp16 A, B and fp32 C.
+
+Exact where the reference test is exact (small-integer operands: every
+product and partial sum is an integer below 2^24, so any correct fp32
+evaluation gives the int64 answer) and within the stated tolerance on seeded
+real-valued data:
+  relative Frobenius error <= 1e-3 and
+  max |error| <= 5e-3 * sqrt(K) * max|a| * max|b|
+against the fp32 CPU oracle on the fp16-rounded inputs.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def module(dev, cudair):
+    from cudair import host
+    m = host.LoadModule(host.KernelsImage())
+    yield m
+    m.Close()
+
+
+@pytest.fixture(autouse=True)
+def no_wait_timeouts(dev, cudair):
+    from cudair import kernels
+    kernels.wait_status(clear=True)
+    yield
+    assert kernels.wait_status(clear=True) == 0
+
+
+def kat(M, N, K):
+    """The TestHopper generator (advanced_test.go:459-463) on an M x K / K x N
+    grid: af = (i+2j)%7-3, bf = (3i+j)%5-2, c = j-i."""
+    i = np.arange(M).reshape(M, 1)
+    k = np.arange(K).reshape(1, K)
+    af = ((i + 2 * k) % 7 - 3)
+    kk = np.arange(K).reshape(K, 1)
+    j = np.arange(N).reshape(1, N)
+    bf = ((3 * kk + j) % 5 - 2)
+    c = (j - i)
+    want = (af.astype(np.int64) @ bf.astype(np.int64) + c).astype(np.float32)
+    return af.astype(np.float32), bf.astype(np.float32), c.astype(np.float32), want
+
+
+def _dev(x, dev, dtype):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev).to(dtype)
+
+
+def test_matmul16_reference_launch_kat64(dev, module, oracle, golden_dir):
+    # TestHopper/MatMul16: n = 64, grid (n/16, n/16), 32 threads, exact ==.
+    import torch
+    from cudair import host
+    n = 64
+    af, bf, c = oracle.matmul16_kat(n)
+    want = np.load(os.path.join(golden_dir, "matmul16_kat64.npz"))["want"]
+    a16 = oracle.f32_to_f16(af)
+    b16 = oracle.f32_to_f16(bf)
+    da = torch.from_numpy(a16.view(np.int16)).to(dev)
+    db = torch.from_numpy(b16.view(np.int16)).to(dev)
+    dc = torch.from_numpy(c).to(dev)
+    torch.cuda.synchronize()
+    module.Function("MatMul16").LaunchEx(
+        host.LaunchConfig(GridX=n // 16, GridY=n // 16, BlockX=32), host.LaunchAttrs(),
+        host.ArgBuffer(da), host.ArgBuffer(db), host.ArgBuffer(dc), host.ArgValue(ctypes.c_int32(n)))
+    got = dc.cpu().numpy()
+    assert np.array_equal(got, want)
+    assert np.array_equal(got, oracle.matmul16(af, bf, c))
+
+
+def test_matmul16_reference_launch_seeded_n256(dev, module, oracle, golden_dir):
+    import torch
+    from cudair import host
+    n = 256
+    a16 = oracle.f32_to_f16(oracle.uniform(n * n, 1)).reshape(n, n)
+    b16 = oracle.f32_to_f16(oracle.uniform(n * n, 2)).reshape(n, n)
+    c = oracle.uniform(n * n, 3).reshape(n, n)
+    af, bf = oracle.f16_to_f32(a16), oracle.f16_to_f32(b16)
+    dc = torch.from_numpy(c).to(dev)
+    da = torch.from_numpy(a16.view(np.int16)).to(dev)
+    db = torch.from_numpy(b16.view(np.int16)).to(dev)
+    torch.cuda.synchronize()
+    module.Function("MatMul16").LaunchEx(
+        host.LaunchConfig(GridX=n // 16, GridY=n // 16, BlockX=32), host.LaunchAttrs(),
+        host.ArgBuffer(da), host.ArgBuffer(db), host.ArgBuffer(dc), host.ArgValue(ctypes.c_int32(n)))
+    got = dc.cpu().numpy()
+    want = oracle.matmul16(af, bf, c)
+    golden = np.load(os.path.join(golden_dir, "matmul16_n256.npz"))["want"]
+    tol_rel, tol_max = oracle.gemm_tolerance(n, np.abs(af).max(), np.abs(bf).max())
+    for ref in (want, golden):
+        rel, mx, bad = oracle.error_norms(got, ref)
+        assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
+
+
+@pytest.mark.parametrize("n", [64, 256, 512, 1024, 2048])
+def test_matmul16_tcgen05_kat_exact(dev, cudair, n):
+    import torch
+    from cudair import kernels
+    af, bf, c, want = kat(n, n, n)
+    da, db, dc = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16), _dev(c, dev, torch.float32)
+    kernels.matmul16(da, db, dc)
+    got = dc.cpu().numpy()
+    bad = np.argwhere(got != want)
+    assert bad.size == 0, f"{len(bad)} mismatches, first at {tuple(bad[0])}: {got[tuple(bad[0])]} vs {want[tuple(bad[0])]}"
+
+
+def test_matmul16_tcgen05_seeded_n256(dev, cudair, oracle, golden_dir):
+    import torch
+    from cudair import kernels
+    n = 256
+    a16 = oracle.f32_to_f16(oracle.uniform(n * n, 1)).reshape(n, n)
+    b16 = oracle.f32_to_f16(oracle.uniform(n * n, 2)).reshape(n, n)
+    c = oracle.uniform(n * n, 3).reshape(n, n)
+    af, bf = oracle.f16_to_f32(a16), oracle.f16_to_f32(b16)
+    da = torch.from_numpy(a16.view(np.int16)).to(dev).view(torch.float16)
+    db = torch.from_numpy(b16.view(np.int16)).to(dev).view(torch.float16)
+    dc = torch.from_numpy(c).to(dev)
+    kernels.matmul16(da, db, dc)
+    got = dc.cpu().numpy()
+    want = oracle.matmul16(af, bf, c)
+    golden = np.load(os.path.join(golden_dir, "matmul16_n256.npz"))["want"]
+    tol_rel, tol_max = oracle.gemm_tolerance(n, np.abs(af).max(), np.abs(bf).max())
+    for ref in (want, golden):
+        rel, mx, bad = oracle.error_norms(got, ref)
+        assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (1, 8, 8), (7, 16, 24), (128, 256, 64), (129, 264, 72), (200, 264, 136), (300, 1000, 1000),
+    (513, 8, 4096), (16, 14336, 512), (1000, 2056, 520),
+])
+def test_gemm_tcgen05_ragged_kat_exact(dev, cudair, M, N, K):
+    import torch
+    from cudair import kernels
+    af, bf, c, want = kat(M, N, K)
+    da, db, dc = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16), _dev(c, dev, torch.float32)
+    kernels.gemm(da, db, dc)
+    got = dc.cpu().numpy()
+    bad = np.argwhere(got != want)
+    assert bad.size == 0, f"{len(bad)} mismatches, first at {tuple(bad[0])}"
+
+
+def test_gemm_tcgen05_padded_leading_dims(dev, cudair):
+    # lda, ldb, ldc larger than the logical widths; untouched padding.
+    import torch
+    from cudair import kernels
+    M, N, K = 300, 520, 200
+    af, bf, c, want = kat(M, N, K)
+    A = torch.zeros(M, K + 24, dtype=torch.float16, device=dev)
+    B = torch.zeros(K, N + 8, dtype=torch.float16, device=dev)
+    C = torch.full((M, N + 12), -5.0, dtype=torch.float32, device=dev)
+    A[:, :K] = _dev(af, dev, torch.float16)
+    B[:, :N] = _dev(bf, dev, torch.float16)
+    C[:, :N] = _dev(c, dev, torch.float32)
+    kernels.gemm(A[:, :K], B[:, :N], C[:, :N])
+    got = C.cpu().numpy()
+    assert np.array_equal(got[:, :N], want)
+    assert np.all(got[:, N:] == -5.0)
+
+
+def _seeded_normal_f16(oracle, n, seed, std):
+    h = oracle.f32_to_f16(oracle.normal(n, seed, 0.0, std))
+    return h, oracle.f16_to_f32(h)
+
+
+def test_gemm_8192_cube_seeded(dev, cudair, oracle):
+    # The 8192^3 configuration: A, B ~ fp16(N(0,1)/sqrt(8192)), C ~ N(0,1).
+    import torch
+    from cudair import kernels
+    n = 8192
+    a16, af = _seeded_normal_f16(oracle, n * n, 6, 1.0 / np.sqrt(n))
+    b16, bf = _seeded_normal_f16(oracle, n * n, 7, 1.0 / np.sqrt(n))
+    c = oracle.normal(n * n, 8).reshape(n, n)
+    af, bf = af.reshape(n, n), bf.reshape(n, n)
+    da = torch.from_numpy(a16.view(np.int16)).to(dev).view(torch.float16).reshape(n, n)
+    db = torch.from_numpy(b16.view(np.int16)).to(dev).view(torch.float16).reshape(n, n)
+    dc = torch.from_numpy(c).to(dev)
+    kernels.gemm(da, db, dc)
+    torch.cuda.synchronize()
+    got = dc.cpu().numpy()
+    tol_rel, tol_max = oracle.gemm_tolerance(n, np.abs(af).max(), np.abs(bf).max())
+    # (1) whole matrix against an fp32 GPU reference of the same op.
+    ref = (da.float() @ db.float()).add_(torch.from_numpy(c).to(dev)).cpu().numpy()
+    rel, mx, bad = oracle.error_norms(got, ref)
+    assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
+    # (2) sampled rows against the CPU oracle (fp32, every tile row-block hit).
+    rows = np.unique(np.concatenate([np.arange(0, n, 257), [n - 1]]))
+    for r in rows[::4]:
+        want = oracle.gemm_ikj(af, bf, c, rows=(int(r), int(r) + 1))
+        rel, mx, bad = oracle.error_norms(got[r:r + 1], want)
+        assert bad == 0 and rel <= tol_rel and mx <= tol_max, (r, rel, mx)
+
+
+def test_gemm_skinny_decode_shape(dev, cudair, oracle):
+    # M=16, N=14336, K=4096: A ~ N(0,1), B ~ N(0,0.02), C = 0.
+    import torch
+    from cudair import kernels
+    M, N, K = 16, 14336, 4096
+    a16, af = _seeded_normal_f16(oracle, M * K, 9, 1.0)
+    b16, bf = _seeded_normal_f16(oracle, K * N, 10, 0.02)
+    af, bf = af.reshape(M, K), bf.reshape(K, N)
+    c = np.zeros((M, N), dtype=np.float32)
+    da = torch.from_numpy(a16.view(np.int16)).to(dev).view(torch.float16).reshape(M, K)
+    db = torch.from_numpy(b16.view(np.int16)).to(dev).view(torch.float16).reshape(K, N)
+    dc = torch.zeros(M, N, dtype=torch.float32, device=dev)
+    kernels.gemm(da, db, dc)
+    got = dc.cpu().numpy()
+    want = oracle.gemm_ikj(af, bf, c)
+    tol_rel, tol_max = oracle.gemm_tolerance(K, np.abs(af).max(), np.abs(bf).max())
+    rel, mx, bad = oracle.error_norms(got, want)
+    assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
+
+
+def test_gemm_repeated_calls_accumulate(dev, cudair):
+    # C = A.B + C is not idempotent: two calls add the product twice.
+    import torch
+    from cudair import kernels
+    M, N, K = 256, 512, 320
+    af, bf, c, want1 = kat(M, N, K)
+    da, db, dc = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16), _dev(c, dev, torch.float32)
+    kernels.gemm(da, db, dc)
+    kernels.gemm(da, db, dc)
+    want2 = want1 + (want1 - c)
+    assert np.array_equal(dc.cpu().numpy(), want2)
