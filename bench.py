@@ -353,6 +353,86 @@ def workload_config(n_gpus):
 # ---- our arm -------------------------------------------------------------------------
 
 
+def run_e2e(args, world, dev, a, b, c, flops, kernels):
+    """The GEMM step through the C ABI from pinned host buffers: H2D of A, B
+    and C, the launch, D2H of C, all inside the timed region."""
+    import torch
+    a_h = a.cpu().pin_memory()
+    b_h = b.cpu().pin_memory()
+    c_h = c.cpu().pin_memory()
+    c_out = torch.empty_like(c_h).pin_memory()
+    a_d, b_d, c_d = torch.empty_like(a), torch.empty_like(b), torch.empty_like(c)
+
+    def e2e_step():
+        a_d.copy_(a_h, non_blocking=True)
+        b_d.copy_(b_h, non_blocking=True)
+        c_d.copy_(c_h, non_blocking=True)
+        kernels.gemm(a_d, b_d, c_d)
+        c_out.copy_(c_d, non_blocking=True)
+
+    steps = max(3, min(args.steps, 20))
+    ms = time_steps(e2e_step, steps, 3, world, dev)
+    return {"value": flops * world / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": a_h.numel() * 2 + b_h.numel() * 2 + c_h.numel() * 4,
+            "d2h_bytes_per_step": c_out.numel() * 4, "ms_per_step": ms, "steps": steps}
+
+
+def run_gather(world, dev, M, N):
+    """Optional reassembly of C on every GPU with NCCL all-gather (not part of
+    the step; timed on its own)."""
+    import torch
+    import torch.distributed as dist
+    c = torch.zeros(M, N, dtype=torch.float32, device=dev)
+    full = torch.empty(world * M, N, dtype=torch.float32, device=dev)
+    t = time_steps(lambda: dist.all_gather_into_tensor(full, c), 3, 3, world, dev)
+    out = {"ms": t, "bytes_received_per_gpu": (world - 1) * M * N * 4,
+           "GB/s_per_gpu": (world - 1) * M * N * 4 / (t * 1e-3) / 1e9}
+    del full, c
+    return out
+
+
+def run_vecadd(args, world, rank, dev, g, kernels):
+    """VecAdd over n = 2^28 fp32 per GPU (3 GiB of traffic per step, > L2)."""
+    import torch
+    g.manual_seed(4000 + rank)
+    va = torch.rand(VEC_N, generator=g, device=dev) * 2 - 1
+    vb = torch.rand(VEC_N, generator=g, device=dev) * 2 - 1
+    vo = torch.empty_like(va)
+    ms = time_steps(lambda: kernels.vecadd(va, vb, vo), args.steps, args.warmup, world, dev)
+    del va, vb, vo
+    return ms, 3 * 4 * VEC_N / (ms * 1e-3) / 1e9
+
+
+def run_skinny(args, world, rank, dev, g, kernels):
+    """M=16, N=14336, K=4096 (decode-shaped): B is 117 MB and is streamed from
+    HBM each step (a 256 MiB write between steps evicts it from L2); each step
+    is timed alone with events around the launch."""
+    import torch
+    sm, sn, sk = SKINNY
+    g.manual_seed(9000 + rank)
+    sa = torch.randn(sm, sk, generator=g, device=dev).half()
+    sb = (torch.randn(sk, sn, generator=g, device=dev) * 0.02).half()
+    sc = torch.zeros(sm, sn, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        kernels.gemm(sa, sb, sc)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(max(5, min(args.steps, 50))):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        kernels.gemm(sa, sb, sc)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = max_over_ranks(statistics.mean(times), world, dev)
+    gbs = (sk * sn * 2 + sm * sk * 2 + 2 * sm * sn * 4) / (ms * 1e-3) / 1e9
+    del sa, sb, sc, flush
+    return ms, gbs
+
+
 def run_ours(args, world, rank, local):
     import torch
     from cudair import kernels
@@ -361,8 +441,18 @@ def run_ours(args, world, rank, local):
     peaks, peak_kind = load_peaks()
     traffic = load_traffic()
     g = torch.Generator(device=dev)
+    only = args.workload
 
-    # -- inputs in HBM
+    if only == "vecadd":
+        v_ms, v_gbs = run_vecadd(args, world, rank, dev, g, kernels)
+        log(f"rank {rank}: vecadd {v_ms:.4f} ms/step {v_gbs:.1f} GB/s")
+        return
+    if only == "skinny":
+        s_ms, s_gbs = run_skinny(args, world, rank, dev, g, kernels)
+        log(f"rank {rank}: skinny {s_ms:.4f} ms {s_gbs:.1f} GB/s")
+        return
+
+    # -- the row-sharded GEMM: inputs resident in HBM
     M, N, K = ROWS_PER_GPU, N_DIM, K_DIM
     g.manual_seed(6000 + rank)
     a = (torch.randn(M, K, generator=g, device=dev) / math.sqrt(K)).half()
@@ -377,87 +467,21 @@ def run_ours(args, world, rank, local):
 
     flops = 2.0 * M * N * K
     sampler = ClockSampler(local)
-    step = lambda: kernels.gemm(a, b, c)  # noqa: E731
-    ms = time_steps(step, args.steps, args.warmup, world, dev, sampler)
+    ms = time_steps(lambda: kernels.gemm(a, b, c), args.steps, args.warmup, world, dev, sampler)
     clocks = sampler.summary()
     kernels.wait_status(clear=True)
-    value = flops * world / (ms * 1e-3) / 1e12
-    per_gpu = flops / (ms * 1e-3) / 1e12
-    log(f"rank {rank}: gemm {ms:.4f} ms/step, {per_gpu:.1f} TFLOP/s per GPU")
+    achieved = flops / (ms * 1e-3) / 1e12
+    log(f"rank {rank}: gemm {ms:.4f} ms/step, {achieved:.1f} TFLOP/s per GPU")
+    if only == "gemm":
+        return
 
-    # -- e2e: host buffers, copies inside the timed region
-    a_h = a.cpu().pin_memory()
-    b_h = b.cpu().pin_memory()
-    c_h = c.cpu().pin_memory()
-    c_out = torch.empty_like(c_h).pin_memory()
-    a_d, b_d, c_d = torch.empty_like(a), torch.empty_like(b), torch.empty_like(c)
-
-    def e2e_step():
-        a_d.copy_(a_h, non_blocking=True)
-        b_d.copy_(b_h, non_blocking=True)
-        c_d.copy_(c_h, non_blocking=True)
-        kernels.gemm(a_d, b_d, c_d)
-        c_out.copy_(c_d, non_blocking=True)
-
-    e2e_steps = max(3, min(args.steps, 20))
-    e2e_ms = time_steps(e2e_step, e2e_steps, max(3, min(args.warmup, 3)), world, dev)
-    e2e_value = flops * world / (e2e_ms * 1e-3) / 1e12
-    h2d = a_h.numel() * 2 + b_h.numel() * 2 + c_h.numel() * 4
-    d2h = c_out.numel() * 4
-    del a_h, b_h, c_h, c_out, a_d, b_d, c_d
-
-    # -- optional all-gather of C (reassembly; not part of the step)
-    gather = None
-    if args.gather and world > 1:
-        import torch.distributed as dist
-        full = torch.empty(world * M, N, dtype=torch.float32, device=dev)
-        dist.all_gather_into_tensor(full, c)
-        torch.cuda.synchronize()
-        t = time_steps(lambda: dist.all_gather_into_tensor(full, c), 3, 1, world, dev)
-        gather = {"ms": t, "bytes_received_per_gpu": (world - 1) * M * N * 4,
-                  "GB/s_per_gpu": (world - 1) * M * N * 4 / (t * 1e-3) / 1e9}
-        del full
-
-    # -- secondary: VecAdd 2^28 per GPU
+    e2e = run_e2e(args, world, dev, a, b, c, flops, kernels)
+    del a, b, c
     torch.cuda.empty_cache()
-    g.manual_seed(4000 + rank)
-    va = torch.rand(VEC_N, generator=g, device=dev) * 2 - 1
-    vb = torch.rand(VEC_N, generator=g, device=dev) * 2 - 1
-    vo = torch.empty_like(va)
-    v_ms = time_steps(lambda: kernels.vecadd(va, vb, vo), args.steps, args.warmup, world, dev)
-    v_bytes = 3 * 4 * VEC_N
-    v_gbs = v_bytes / (v_ms * 1e-3) / 1e9
-    del va, vb, vo
-
-    # -- secondary: decode-shaped GEMM (memory-bound on B)
+    gather = run_gather(world, dev, M, N) if (args.gather and world > 1) else None
+    v_ms, v_gbs = run_vecadd(args, world, rank, dev, g, kernels)
     sm, sn, sk = SKINNY
-    g.manual_seed(9000 + rank)
-    sa = torch.randn(sm, sk, generator=g, device=dev).half()
-    sb = (torch.randn(sk, sn, generator=g, device=dev) * 0.02).half()
-    sc = torch.zeros(sm, sn, device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MiB > L2
-
-    def skinny_step():
-        flush.zero_()  # evicts B from L2 so each step streams it from HBM
-        kernels.gemm(sa, sb, sc)
-
-    # time the GEMM alone with events around it, flushing between steps
-    for _ in range(args.warmup):
-        skinny_step()
-    torch.cuda.synchronize()
-    s_times = []
-    for _ in range(max(5, min(args.steps, 50))):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        kernels.gemm(sa, sb, sc)
-        e1.record()
-        torch.cuda.synchronize()
-        s_times.append(e0.elapsed_time(e1))
-    s_ms = max_over_ranks(statistics.mean(s_times), world, dev)
-    s_bytes = sk * sn * 2 + sm * sk * 2 + 2 * sm * sn * 4
-    s_gbs = s_bytes / (s_ms * 1e-3) / 1e9
-    del sa, sb, sc, flush
+    s_ms, s_gbs = run_skinny(args, world, rank, dev, g, kernels)
     kernels.wait_status(clear=True)
 
     # -- CPU baseline (rank 0, N = 1 only)
@@ -472,9 +496,8 @@ def run_ours(args, world, rank, local):
     if rank != 0:
         return
     tensor_peak = peaks["bf16_tflops"]
-    achieved = flops / (ms * 1e-3) / 1e12
     line = {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "metric": METRIC, "value": achieved * world, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,1)/sqrt(8192) fp16 operands, N(0,1) fp32 C)",
@@ -484,8 +507,7 @@ def run_ours(args, world, rank, local):
                      "traffic": traffic.get("gemm_8192"),
                      "peak_kind": f"{peak_kind} bf16 burst (fp16 dense rate is equal)",
                      "frac_of_nominal": achieved / 2250.0},
-        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "e2e": e2e,
         "cpu_baseline": cpu,
         "gpu_launches": args.steps * world,
         "clocks": clocks,
@@ -514,6 +536,8 @@ def main():
     ap.add_argument("--gather", action="store_true", help="also all-gather C over NCCL (timed apart)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds for the CPU baseline")
+    ap.add_argument("--workload", choices=["all", "gemm", "vecadd", "skinny"], default="all",
+                    help="run one part only (for profiling); the JSON line needs 'all'")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -130,7 +130,7 @@ def ArgValue(v) -> Arg:
 def ArgBuffer(t) -> Arg:
     """Passes a device buffer's pointer (ArgBuffer[T]); t is a torch tensor or an int."""
     ptr = t if isinstance(t, int) else t.data_ptr()
-    return Arg(ctypes.c_uint64(ptr))
+    return Arg(bytes(ctypes.c_uint64(ptr)))
 
 
 def ArgBytes(p: bytes) -> Arg:
