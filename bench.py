@@ -19,7 +19,8 @@ the device-timed step).  `e2e` times the same step through the C ABI with
 host buffers: pinned host -> device copies of A, B, C, the launch, and the
 device -> host copy of C, all inside the timed region.  The line also
 carries VecAdd (n = 2^28 fp32 per GPU, HBM-bound) and the decode-shaped GEMM
-(M=16, N=14336, K=4096) as secondary results, each against its roofline.
+(M=16, N=14336, K=4096, three copies of B cycled so each step reads B from
+HBM) as secondary results, each against its roofline.
 
 `--impl reference` times the reference's CPU implementation of the path (the
 i-j-k float32 loop of its tests, restated in C under oracle/) on all host
@@ -181,13 +182,8 @@ def dist_setup(args):
 
 
 def max_over_ranks(x: float, world: int, dev) -> float:
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from cudair import multigpu
+    return multigpu.max_over_ranks(x, world, dev)
 
 
 def barrier(world):
@@ -234,40 +230,13 @@ class _Null:
 
 
 def replicate_b(b, world, rank, dev):
-    """Copies rank 0's B into every other rank's local B over NVLink: rank 0
-    exports its allocation (CUDA IPC), the others map it, copy it into local
-    HBM with one device-to-device copy and unmap it.  Returns the max copy
-    time over ranks in ms."""
-    if world == 1:
-        return 0.0
-    import ctypes
-    import torch
-    import torch.distributed as dist
-    from cudair import _lib
-    L = _lib.lib()
-    handle = (ctypes.c_uint8 * 64)()
-    if rank == 0:
-        _lib.check(L.cudair_ipc_export(ctypes.c_void_p(b.data_ptr()), handle))
-    handles = [None] * world
-    dist.all_gather_object(handles, bytes(handle) if rank == 0 else None)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    ms = 0.0
-    if rank != 0:
-        h = (ctypes.c_uint8 * 64).from_buffer_copy(handles[0])
-        peer = ctypes.c_void_p()
-        _lib.check(L.cudair_ipc_open(h, ctypes.byref(peer)))
-        s = torch.cuda.current_stream()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record()
-        _lib.check(L.cudair_peer_copy(ctypes.c_void_p(b.data_ptr()), peer, b.numel() * b.element_size(),
-                                      ctypes.c_void_p(s.cuda_stream)))
-        ev1.record()
-        torch.cuda.synchronize()
-        ms = ev0.elapsed_time(ev1)
-        _lib.check(L.cudair_ipc_close(peer))
-    dist.barrier()
-    log(f"rank {rank}: B replicated in {ms:.3f} ms (wall {1e3 * (time.perf_counter() - t0):.1f} ms)")
+    """Copies rank 0's B into every other rank's local B over NVLink (CUDA IPC
+    export on rank 0, map + one device-to-device copy + unmap elsewhere);
+    returns the max copy time over ranks in ms."""
+    from cudair import multigpu
+    ms = multigpu.replicate_from_rank0(b, rank, world)
+    if world > 1:
+        log(f"rank {rank}: B replicated in {ms:.3f} ms")
     return max_over_ranks(ms, world, dev)
 
 
@@ -404,32 +373,31 @@ def run_vecadd(args, world, rank, dev, g, kernels):
 
 
 def run_skinny(args, world, rank, dev, g, kernels):
-    """M=16, N=14336, K=4096 (decode-shaped): B is 117 MB and is streamed from
-    HBM each step (a 256 MiB write between steps evicts it from L2); each step
-    is timed alone with events around the launch."""
+    """M=16, N=14336, K=4096 (decode-shaped): B is 117 MB, so three copies of
+    it are cycled (351 MB > L2) and every step streams its B from HBM; each
+    step is timed alone with events around the launch."""
     import torch
     sm, sn, sk = SKINNY
     g.manual_seed(9000 + rank)
     sa = torch.randn(sm, sk, generator=g, device=dev).half()
-    sb = (torch.randn(sk, sn, generator=g, device=dev) * 0.02).half()
+    sbs = [(torch.randn(sk, sn, generator=g, device=dev) * 0.02).half() for _ in range(3)]
     sc = torch.zeros(sm, sn, device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    for _ in range(args.warmup):
-        flush.zero_()
-        kernels.gemm(sa, sb, sc)
+    for i in range(args.warmup):
+        kernels.gemm(sa, sbs[i % 3], sc)
     torch.cuda.synchronize()
     times = []
-    for _ in range(max(5, min(args.steps, 50))):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(6, min(args.steps, 60))
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+    for i, (e0, e1) in enumerate(events):
         e0.record()
-        kernels.gemm(sa, sb, sc)
+        kernels.gemm(sa, sbs[i % 3], sc)
         e1.record()
-        torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1))
-    ms = max_over_ranks(statistics.mean(times), world, dev)
+    torch.cuda.synchronize()
+    times = [e0.elapsed_time(e1) for e0, e1 in events]
+    ms = max_over_ranks(statistics.median(times), world, dev)
     gbs = (sk * sn * 2 + sm * sk * 2 + 2 * sm * sn * 4) / (ms * 1e-3) / 1e9
-    del sa, sb, sc, flush
+    del sa, sbs, sc
     return ms, gbs
 
 

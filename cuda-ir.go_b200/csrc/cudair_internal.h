@@ -64,6 +64,11 @@ int encode_tiled_internal(CUtensorMap *out, uint32_t data_type, uint32_t rank,
 
 int sm_count_current_device(int *count);
 
+int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int K, int64_t lda,
+                       int64_t ldb, int64_t ldc, int sm_count, unsigned int *status,
+                       cudaStream_t stream);
+int skinny_reset_workspace();
+
 int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K,
                        int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t stream);
 

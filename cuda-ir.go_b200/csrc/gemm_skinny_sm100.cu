@@ -1,0 +1,398 @@
+// gemm_skinny_sm100.cu - the same C = A.B + C for few rows (M <= 64: the
+// decode-shaped GEMM, e.g. M = 16, N = 14336, K = 4096), where the
+// square-tile kernels leave most SMs idle and the time is the one pass over
+// B (K x N fp16) through HBM.
+//
+// Design:
+//   * swap of operands: D^T (N x M) = B^T . A^T, so the 128-row side of
+//     tcgen05.mma (M = 128) runs over N and the small M becomes the MMA's N
+//     (mpad = M rounded up to 16).  B is read MN-major exactly as stored, A
+//     K-major; the accumulator is 128 TMEM lanes (n) x mpad columns (m).
+//   * stream-K: the (n-tile x 64-wide k-block) space is cut into one
+//     contiguous range per CTA, one CTA per SM, so every SM streams the same
+//     share of B however N and K divide.  A range covers whole n-tiles
+//     (written straight into C) and at most two partial ones.
+//   * deterministic fix-up: a partial n-tile's contributors store their
+//     fp32 partials in a workspace, count themselves on the tile's counter,
+//     and the last to arrive adds C and the partials in CTA order (so the sum
+//     order, and the result, do not depend on timing), stores C and resets
+//     the counter to zero for the next launch.
+//   * an 8-stage TMA ring of 16 KB B tiles (two 64 x 64 boxes) plus
+//     mpad x 64 A tiles keeps about 180 KB of B in flight per SM.
+//
+// Roles as in gemm_sm100.cu (192 threads): warp 0 TMA producer, warp 1 TMEM
+// owner and MMA issuer, warps 2-5 epilogue and fix-up.  All waits are
+// bounded.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "cudair_internal.h"
+#include "sm100.cuh"
+
+namespace cudair {
+
+namespace skinny {
+
+constexpr int BN_T = 128;  // n per tile (the MMA's M)
+constexpr int BK = 64;
+constexpr int STAGES = 8;
+constexpr int THREADS = 192;
+constexpr int MAX_M = 64;
+constexpr uint32_t B_BOX_BYTES = 64 * BK * 2;        // 64 n x 64 k
+constexpr uint32_t B_STAGE_BYTES = 2 * B_BOX_BYTES;  // 16 KB
+constexpr uint32_t A_STAGE_MAX = MAX_M * BK * 2;     // 8 KB at mpad = 64
+constexpr uint32_t BAR_BYTES = 256;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (B_STAGE_BYTES + A_STAGE_MAX) + BAR_BYTES;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+
+// Workspace layout: tile counters first, then two partial slots per CTA.
+constexpr size_t COUNTER_BYTES = 256 * 1024;  // 65536 n-tiles
+constexpr int MAX_TILES = COUNTER_BYTES / 4;
+constexpr size_t partial_bytes(int grid, int mpad) {
+    return static_cast<size_t>(grid) * 2 * BN_T * mpad * 4;
+}
+
+struct Range {
+    long long start, end;  // [start, end) in k-block units
+};
+
+__device__ __forceinline__ long long range_start(int c, long long T, int G) {
+    return (static_cast<long long>(c) * T) / G;
+}
+// The CTA whose range contains k-block unit x.
+__device__ __forceinline__ int cta_of(long long x, long long T, int G) {
+    return static_cast<int>(((x + 1) * G - 1) / T);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA,
+                       float *__restrict__ C, int M, int N, int K, long long ldc, int mpad,
+                       unsigned int *__restrict__ counters, float *__restrict__ partials,
+                       unsigned int *status) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+    const uint32_t a_stage_bytes = static_cast<uint32_t>(mpad) * BK * 2;  // multiple of 1024
+    uint8_t *sB = smem;
+    uint8_t *sA = smem + STAGES * B_STAGE_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sA + STAGES * A_STAGE_MAX);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + STAGES;
+    uint64_t *acc_full = bars + 2 * STAGES;
+    uint64_t *acc_empty = acc_full + 2;
+    uint64_t *drain = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    volatile int *last_flag = abort_flag + 1;
+
+    const uint32_t warp = warp_id(), lane = lane_id();
+    const int n_tiles = (N + BN_T - 1) / BN_T;
+    const int num_kb = (K + BK - 1) / BK;
+    const long long T = static_cast<long long>(n_tiles) * num_kb;
+    const int G = static_cast<int>(gridDim.x);
+    const int c = static_cast<int>(blockIdx.x);
+    const long long r0 = range_start(c, T, G), r1 = range_start(c + 1, T, G);
+    const uint32_t tmem_cols = mpad <= 16 ? 32u : (mpad <= 32 ? 64u : 128u);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_map(&tmA);
+        tma_prefetch_map(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const uint64_t policy_b = l2_policy_evict_normal();
+            const uint64_t policy_a = l2_policy_evict_last();  // A is re-read by every CTA
+            uint32_t stage = 0, phase = 0, issued = 0;
+            bool ok = true;
+            for (long long x = r0; x < r1 && ok; ++x) {
+                const int t = static_cast<int>(x / num_kb), kb = static_cast<int>(x % num_kb);
+                const int n0 = t * BN_T, k0 = kb * BK;
+                const int nb = (n0 + 64 < N) ? 2 : 1;  // skip a box wholly beyond N
+                if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, kSiteProducerEmpty)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[stage], nb * B_BOX_BYTES + a_stage_bytes);
+                for (int j = 0; j < nb; ++j)
+                    tma_load_2d(sB + stage * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB, &full[stage],
+                                n0 + 64 * j, k0, policy_b);
+                tma_load_2d(sA + stage * A_STAGE_MAX, &tmA, &full[stage], k0, 0, policy_a);
+                ++issued;
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                const uint32_t outstanding = issued < STAGES ? issued : STAGES;
+                for (uint32_t i = 1; i <= outstanding; ++i) {
+                    const uint32_t idx = issued - i;
+                    int never = 0;
+                    mbar_wait(&full[idx % STAGES], (idx / STAGES) & 1u, &never, status, kSiteDrain);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_f32(BN_T, static_cast<uint32_t>(mpad), true, false);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true, issued_any = false;
+            long long x = r0;
+            while (x < r1 && ok) {
+                const int t = static_cast<int>(x / num_kb);
+                const long long seg_end = min(r1, static_cast<long long>(t + 1) * num_kb);
+                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, status, kSiteMmaAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after_sync();
+                const uint32_t d_tmem = tmem_base + acc * static_cast<uint32_t>(mpad);
+                bool first = true;
+                for (; x < seg_end; ++x) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, status, kSiteMmaFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
+                    const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
+                    const uint32_t a_base = smem_u32(sA + stage * A_STAGE_MAX);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        // B^T: MN-major, n-blocks 8 KB apart, k groups 1 KB apart.
+                        const uint64_t b_desc = smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
+                        // A^T: K-major rows of 128 B (one per m).
+                        const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                        umma_f16_ss(d_tmem, b_desc, a_desc, idesc, (first && kk == 0) ? 0u : 1u);
+                    }
+                    first = false;
+                    issued_any = true;
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[acc]);
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            if (!ok && issued_any) {
+                umma_commit(drain);
+                int never = 0;
+                mbar_wait(drain, 0, &never, status, kSiteDrain);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue and fix-up (warps 2..5) ----------------
+        const uint32_t q = warp & 3u;
+        const int nl = static_cast<int>(q * 32 + lane);  // n within the tile
+        const bool leader = (warp == 2 && lane == 0);
+        uint32_t acc = 0, acc_phase = 0;
+        long long x = r0;
+        while (x < r1) {
+            const int t = static_cast<int>(x / num_kb);
+            const long long tile_lo = static_cast<long long>(t) * num_kb, tile_hi = tile_lo + num_kb;
+            const long long seg_end = min(r1, tile_hi);
+            const bool whole = (x == tile_lo && seg_end == tile_hi);
+            const int slot = (x == r0) ? 0 : 1;  // a partial segment is the range's first or last
+            x = seg_end;
+            const int n = t * BN_T + nl;
+            // The four warps decide together whether to go on: a warp that
+            // gave up has raised the abort flag before this barrier.
+            const bool ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull);
+            named_bar_sync(1, 128);
+            if (!ok || *abort_flag) break;
+            tc_fence_after_sync();
+            const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * static_cast<uint32_t>(mpad);
+            float *part = partials + (static_cast<size_t>(c) * 2 + slot) * BN_T * mpad;
+            for (int j = 0; j < mpad / 16; ++j) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(t_row + 16 * j, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int m = 16 * j + i;
+                    if (whole) {
+                        if (m < M && n < N) {
+                            float *p = C + static_cast<long long>(m) * ldc + n;
+                            *p = *p + __uint_as_float(r[i]);
+                        }
+                    } else {
+                        part[m * BN_T + nl] = __uint_as_float(r[i]);
+                    }
+                }
+            }
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
+            if (whole) continue;
+
+            // Partial tile: count in; the last contributor reduces in CTA order.
+            __threadfence();
+            named_bar_sync(1, 128);
+            const int c_lo = cta_of(tile_lo, T, G), c_hi = cta_of(tile_hi - 1, T, G);
+            if (leader) {
+                const unsigned int prev = atomicAdd(&counters[t], 1u);
+                *last_flag = (prev == static_cast<unsigned int>(c_hi - c_lo)) ? 1 : 0;
+            }
+            named_bar_sync(1, 128);
+            if (*last_flag) {
+                __threadfence();
+                if (n < N) {
+                    for (int m = 0; m < M; ++m) {
+                        float *p = C + static_cast<long long>(m) * ldc + n;
+                        float v = *p;
+                        for (int cc = c_lo; cc <= c_hi; ++cc) {
+                            const long long s_cc = range_start(cc, T, G);
+                            const int sl = (s_cc / num_kb == t) ? 0 : 1;
+                            const float *pc = partials + (static_cast<size_t>(cc) * 2 + sl) * BN_T * mpad;
+                            v += __ldcg(pc + m * BN_T + nl);
+                        }
+                        *p = v;
+                    }
+                }
+                if (leader) counters[t] = 0u;
+            }
+            named_bar_sync(1, 128);  // last_flag is reused by the next partial tile
+        }
+        __syncwarp();
+    }
+
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem_base, tmem_cols);
+    }
+}
+
+}  // namespace skinny
+
+namespace {
+
+struct Workspace {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    bool attr_set = false;
+};
+std::mutex g_ws_mu;
+Workspace g_ws[64];
+
+constexpr size_t kWorkspaceBytes = 16u << 20;
+
+// The library's per-device workspace of the skinny kernel (tile counters +
+// partial slots), allocated and zeroed on the first call on a device.
+int workspace(Workspace **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return set_error(CUDAIR_ERR_INVALID, "cudair: device index %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    Workspace &w = g_ws[dev];
+    if (!w.ptr) {
+        e = cudaMalloc(&w.ptr, kWorkspaceBytes);
+        if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(skinny workspace)");
+        e = cudaMemset(w.ptr, 0, kWorkspaceBytes);
+        if (e != cudaSuccess) return cuda_error(e, "cudaMemset(skinny workspace)");
+        w.bytes = kWorkspaceBytes;
+    }
+    if (!w.attr_set) {
+        e = cudaFuncSetAttribute(skinny::gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(skinny::SMEM_BYTES));
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(skinny)");
+        w.attr_set = true;
+    }
+    *out = &w;
+    return CUDAIR_OK;
+}
+
+}  // namespace
+
+// Called after a bounded wait gave up: a launch that unwound early may have
+// left tile counters raised, so they are zeroed before the next launch.
+int skinny_reset_workspace() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return CUDAIR_OK;
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    if (g_ws[dev].ptr) {
+        cudaError_t e = cudaMemset(g_ws[dev].ptr, 0, g_ws[dev].bytes);
+        if (e != cudaSuccess) return cuda_error(e, "cudaMemset(skinny workspace)");
+    }
+    return CUDAIR_OK;
+}
+
+int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int K, int64_t lda,
+                       int64_t ldb, int64_t ldc, int sm_count, unsigned int *status,
+                       cudaStream_t stream) {
+    if (M < 1 || M > skinny::MAX_M)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: the few-row kernel takes 1 <= M <= %d, got %d",
+                         skinny::MAX_M, M);
+    const int n_tiles = (N + skinny::BN_T - 1) / skinny::BN_T;
+    if (n_tiles > skinny::MAX_TILES)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: N = %d too large for the few-row kernel", N);
+    Workspace *ws = nullptr;
+    int rc = workspace(&ws);
+    if (rc != CUDAIR_OK) return rc;
+    const int mpad = (M + 15) / 16 * 16;
+
+    alignas(64) CUtensorMap tmB, tmA;
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+        const uint32_t box[2] = {64, skinny::BK};
+        rc = encode_tiled_internal(&tmB, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(b),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+        const uint32_t box[2] = {skinny::BK, static_cast<uint32_t>(mpad)};
+        rc = encode_tiled_internal(&tmA, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(a),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    const long long T = static_cast<long long>(n_tiles) * ((K + skinny::BK - 1) / skinny::BK);
+    const int grid = static_cast<int>(T < sm_count ? T : sm_count);
+    unsigned int *counters = static_cast<unsigned int *>(ws->ptr);
+    float *partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws->ptr) + skinny::COUNTER_BYTES);
+    skinny::gemm_skinny_kernel<<<grid, skinny::THREADS, skinny::SMEM_BYTES, stream>>>(
+        tmB, tmA, c, M, N, K, static_cast<long long>(ldc), mpad, counters, partials, status);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch");
+    return CUDAIR_OK;
+}
+
+}  // namespace cudair

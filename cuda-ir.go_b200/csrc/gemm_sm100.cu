@@ -1,33 +1,46 @@
 // gemm_sm100.cu - C = A.B + C with fp16 A (M x K, row-major), fp16 B
 // (K x N, row-major), fp32 C (M x N) updated in place, fp32 accumulation:
 // the operation of MatMul16 (examples/hopper/hopper.go:194-226) for any
-// M, N, K, as a persistent, warp-specialised tcgen05 kernel for sm_100a.
+// M, N, K, as persistent, warp-specialised tcgen05 kernels for sm_100a.
 //
-// Design (one CTA per SM, 192 threads):
-//   warp 0     TMA producer: one thread streams 128x64 A tiles and 64x256 B
-//              tiles (four 64x64 boxes) into a 4-stage shared-memory ring with
-//              128-byte swizzle, each stage completing on a `full` mbarrier.
-//   warp 1     MMA issuer: allocates 512 TMEM columns (two 128x256 fp32
-//              accumulators), and one thread issues tcgen05.mma.kind::f16
-//              (M=128, N=256, K=16) from shared-memory descriptors: A K-major,
-//              B MN-major (B is read as stored; no transpose pass).  Each stage
-//              is released with tcgen05.commit on its `empty` mbarrier; a
-//              finished accumulator is announced on `acc_full`.
-//   warps 2-5  epilogue: each warp owns the 32 TMEM lanes (rows) of its
-//              quarter, reads 32 columns at a time with tcgen05.ld, adds C
-//              from global memory and stores the sum; the accumulator is handed
-//              back on `acc_empty`, so the epilogue of tile i overlaps the
-//              mainloop of tile i+1.
-// Tiles are visited in groups of 16 row-blocks so the CTAs resident at one
+// Two variants share the roles, the tile order and the epilogue:
+//
+//   pair (default for M > 128): clusters of two CTAs on two SMs compute
+//     256 x 256 tiles with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16).
+//     Each CTA loads its own 128 rows of A and its own 128 columns of B (no
+//     multicast), so a CTA moves 32 KB per 64-wide k-block instead of 48 KB;
+//     seven 32 KB stages fit in shared memory.  The even CTA issues the MMAs.
+//   single (M <= 128): one CTA per SM computes 128 x 256 tiles with
+//     tcgen05.mma.cta_group::1 from a four-stage ring of 48 KB stages.
+//
+// Roles (192 threads per CTA):
+//   warp 0     TMA producer (one thread): A boxes of 128 x 64 and B boxes of
+//              64 (n) x 64 (k), 128-byte swizzle, completing on a `full`
+//              mbarrier with expect-tx (for a pair, the even CTA's barrier
+//              counts both CTAs' bytes).
+//   warp 1     TMEM owner (512 columns: two 256-column fp32 accumulators) and
+//              MMA issuer (one thread).  A is read K-major, B MN-major exactly
+//              as stored; tcgen05.commit releases each stage on `empty` and
+//              announces a finished accumulator on `acc_full` (multicast to
+//              both CTAs of a pair).
+//   warps 2-5  epilogue: warp w owns TMEM lanes 32 (w mod 4) .. +31 (one row
+//              per thread), reads 32 columns at a time with tcgen05.ld, adds C
+//              (its 16-byte loads issued one chunk ahead, the first before
+//              the accumulator is ready) and stores the sum; the accumulator
+//              is handed back on `acc_empty` (for a pair, the even CTA's,
+//              counting the eight epilogue warps of both CTAs), so tile i's
+//              epilogue overlaps tile i+1's mainloop.
+// Tiles are visited in groups of row-blocks so that the CTAs resident at one
 // time share A row-panels and B column-panels in L2.
 //
 // Every mbarrier wait is bounded (sm100.cuh, mbar_wait): a wait that gives up
-// records its site in g_wait_status, raises the CTA's abort flag, and all
-// roles unwind; the producer first waits (bounded) for its copies in flight,
-// the MMA thread for its MMAs, and TMEM is always freed before exit.
+// records its site in g_wait_status and raises the abort flag (of both CTAs
+// of a pair); all roles unwind, in-flight copies and MMAs are waited for
+// (with limits), and TMEM is always freed before exit.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "cudair_internal.h"
@@ -39,27 +52,37 @@ __device__ unsigned int g_wait_status;
 
 namespace gemm {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 64;
-constexpr int STAGES = 4;
-constexpr int GROUP_M = 16;
+constexpr int BN = 256;  // N per tile (and per MMA)
+constexpr int BK = 64;   // K per stage: one 128-byte swizzle row of fp16
 constexpr int THREADS = 192;
-constexpr uint32_t A_STAGE_BYTES = BM * BK * 2;  // 16 KB
-constexpr uint32_t B_BOX_BYTES = 64 * BK * 2;    // 8 KB: 64 n x 64 k
-constexpr uint32_t B_STAGE_BYTES = BN * BK * 2;  // 32 KB
-constexpr uint32_t STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
-constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
+constexpr uint32_t A_BOX_BYTES = 128 * BK * 2;  // 16 KB: 128 rows x 64 k
+constexpr uint32_t B_BOX_BYTES = 64 * BK * 2;   // 8 KB: 64 n x 64 k
+constexpr uint32_t TMEM_COLS = 2 * BN;           // two accumulators
 constexpr uint32_t BAR_BYTES = 256;
-constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+
+// single-CTA variant
+constexpr int S_BM = 128;
+constexpr int S_STAGES = 4;
+constexpr int S_GROUP_M = 16;
+constexpr uint32_t S_STAGE_B = BN / 64 * B_BOX_BYTES;  // 32 KB
+constexpr size_t S_SMEM = 1024 + S_STAGES * (A_BOX_BYTES + S_STAGE_B) + BAR_BYTES;
+
+// CTA-pair variant
+constexpr int P_BM = 256;  // rows per pair tile, 128 per CTA
+constexpr int P_STAGES = 7;
+constexpr int P_GROUP_M = 8;
+constexpr uint32_t P_STAGE_B = BN / 2 / 64 * B_BOX_BYTES;  // 16 KB: this CTA's 128 columns
+constexpr size_t P_SMEM = 1024 + P_STAGES * (A_BOX_BYTES + P_STAGE_B) + BAR_BYTES;
+
+static_assert(S_SMEM <= 227 * 1024 && P_SMEM <= 227 * 1024, "shared memory budget");
 
 // Row-block / column-block of persistent tile index t (grouped raster).
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &m_blk, int &n_blk) {
-    const int per_group = GROUP_M * num_n;
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int &m_blk,
+                                            int &n_blk) {
+    const int per_group = group_m * num_n;
     const int group = t / per_group;
-    const int first_m = group * GROUP_M;
-    const int gsize = min(num_m - first_m, GROUP_M);
+    const int first_m = group * group_m;
+    const int gsize = min(num_m - first_m, group_m);
     const int r = t - group * per_group;
     m_blk = first_m + r % gsize;
     n_blk = r / gsize;
@@ -71,6 +94,66 @@ __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity, unsig
     mbar_wait(bar, parity, &never, status, kSiteDrain);
 }
 
+// 32 columns of C for this thread's row, as eight 16-byte loads.
+__device__ __forceinline__ void load_c_chunk(float4 (&v)[8], const float *crow, int col, int N,
+                                             bool row_ok) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        v[j] = (row_ok && col + 4 * j < N) ? *reinterpret_cast<const float4 *>(crow + col + 4 * j)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// Adds this warp's 32 accumulator rows (TMEM lanes from t_row, 256 columns)
+// to C and stores the sums.  c_next holds chunk 0 of C, loaded by the caller.
+__device__ __forceinline__ void epilogue_rows_vec4(uint32_t t_row, float *crow, int row, int n0,
+                                                   int M, int N, float4 (&c_next)[8]) {
+    const bool row_ok = row < M;
+#pragma unroll
+    for (int ch = 0; ch < BN / 32; ++ch) {
+        float4 c_cur[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) c_cur[j] = c_next[j];
+        if (ch + 1 < BN / 32) load_c_chunk(c_next, crow, n0 + (ch + 1) * 32, N, row_ok);
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + ch * 32, r);
+        tmem_ld_wait();
+        const int col = n0 + ch * 32;
+        if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (col + 4 * j < N) {
+                    float4 v = c_cur[j];
+                    v.x += __uint_as_float(r[4 * j + 0]);
+                    v.y += __uint_as_float(r[4 * j + 1]);
+                    v.z += __uint_as_float(r[4 * j + 2]);
+                    v.w += __uint_as_float(r[4 * j + 3]);
+                    *reinterpret_cast<float4 *>(crow + col + 4 * j) = v;
+                }
+            }
+        }
+    }
+}
+
+// Same, for C whose rows are not 16-byte aligned: scalar accesses.
+__device__ __forceinline__ void epilogue_rows_scalar(uint32_t t_row, float *crow, int row, int n0,
+                                                     int M, int N) {
+#pragma unroll 1
+    for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + ch * 32, r);
+        tmem_ld_wait();
+        const int col = n0 + ch * 32;
+        if (row < M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col + j < N) crow[col + j] += __uint_as_float(r[j]);
+        }
+    }
+}
+
+// =============================================================================
+// Single-CTA variant: 128 x 256 tiles.
+// =============================================================================
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16f32_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, float *__restrict__ C, int M,
@@ -80,25 +163,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // 1024-aligned tiles
 
     uint8_t *sA = smem;
-    uint8_t *sB = smem + STAGES * A_STAGE_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE_BYTES);
+    uint8_t *sB = smem + S_STAGES * A_BOX_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sB + S_STAGES * S_STAGE_B);
     uint64_t *full = bars;
-    uint64_t *empty = bars + STAGES;
-    uint64_t *acc_full = bars + 2 * STAGES;
+    uint64_t *empty = bars + S_STAGES;
+    uint64_t *acc_full = bars + 2 * S_STAGES;
     uint64_t *acc_empty = acc_full + 2;
     uint64_t *drain = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const uint32_t warp = warp_id(), lane = lane_id();
-    const int num_m = (M + BM - 1) / BM;
+    const int num_m = (M + S_BM - 1) / S_BM;
     const int num_n = (N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
     const int num_kb = (K + BK - 1) / BK;
     unsigned int *status = &g_wait_status;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < S_STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -129,12 +212,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 int m_blk, n_blk;
-                tile_coords(t, num_m, num_n, m_blk, n_blk);
-                const int m0 = m_blk * BM, n0 = n_blk * BN;
+                tile_coords(t, num_m, num_n, S_GROUP_M, m_blk, n_blk);
+                const int m0 = m_blk * S_BM, n0 = n_blk * BN;
                 // B boxes that start at or beyond column N are not loaded: the
                 // accumulator columns they would feed are never stored.
                 const int nb = min(BN / 64, (N - n0 + 63) / 64);
-                const uint32_t tx = A_STAGE_BYTES + static_cast<uint32_t>(nb) * B_BOX_BYTES;
+                const uint32_t tx = A_BOX_BYTES + static_cast<uint32_t>(nb) * B_BOX_BYTES;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status,
                                    kSiteProducerEmpty)) {
@@ -143,12 +226,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     mbar_arrive_expect_tx(&full[stage], tx);
                     const int k0 = kb * BK;
-                    tma_load_2d(sA + stage * A_STAGE_BYTES, &tmA, &full[stage], k0, m0, policy);
+                    tma_load_2d(sA + stage * A_BOX_BYTES, &tmA, &full[stage], k0, m0, policy);
                     for (int j = 0; j < nb; ++j)
-                        tma_load_2d(sB + stage * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB,
-                                    &full[stage], n0 + 64 * j, k0, policy);
+                        tma_load_2d(sB + stage * S_STAGE_B + j * B_BOX_BYTES, &tmB, &full[stage],
+                                    n0 + 64 * j, k0, policy);
                     ++issued;
-                    if (++stage == STAGES) {
+                    if (++stage == S_STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -156,10 +239,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             if (!ok) {
                 // Let the copies still in flight land before the CTA exits.
-                const uint32_t outstanding = issued < STAGES ? issued : STAGES;
+                const uint32_t outstanding = issued < S_STAGES ? issued : S_STAGES;
                 for (uint32_t i = 1; i <= outstanding; ++i) {
                     const uint32_t idx = issued - i;
-                    drain_wait(&full[idx % STAGES], (idx / STAGES) & 1u, status);
+                    drain_wait(&full[idx % S_STAGES], (idx / S_STAGES) & 1u, status);
                 }
             }
         }
@@ -167,7 +250,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(BM, BN, false, true);
+            constexpr uint32_t idesc = idesc_f16_f32(S_BM, BN, false, true);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true, issued_any = false;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -184,8 +267,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         break;
                     }
                     tc_fence_after_sync();
-                    const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
-                    const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
+                    const uint32_t a_base = smem_u32(sA + stage * A_BOX_BYTES);
+                    const uint32_t b_base = smem_u32(sB + stage * S_STAGE_B);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         // A: K-major rows of 128 B; +32 B per 16-wide k step.
@@ -197,7 +280,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     issued_any = true;
                     umma_commit(&empty[stage]);
-                    if (++stage == STAGES) {
+                    if (++stage == S_STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -219,41 +302,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t acc = 0, acc_phase = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int m_blk, n_blk;
-            tile_coords(t, num_m, num_n, m_blk, n_blk);
-            const int m0 = m_blk * BM, n0 = n_blk * BN;
+            tile_coords(t, num_m, num_n, S_GROUP_M, m_blk, n_blk);
+            const int m0 = m_blk * S_BM, n0 = n_blk * BN;
+            const int row = m0 + static_cast<int>(q * 32 + lane);
+            float *crow = C + static_cast<long long>(row) * ldc;
+            float4 c_next[8];
+            if (vec4) load_c_chunk(c_next, crow, n0, N, row < M);
             if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull))
                 break;
             tc_fence_after_sync();
-            const int row = m0 + static_cast<int>(q * 32 + lane);
             const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
-            float *crow = C + static_cast<long long>(row) * ldc;
-#pragma unroll 1
-            for (int ch = 0; ch < BN / 32; ++ch) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(t_row + ch * 32, r);
-                tmem_ld_wait();
-                const int col = n0 + ch * 32;
-                if (row < M && col < N) {
-                    if (vec4) {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            if (col + 4 * j < N) {
-                                float4 *p = reinterpret_cast<float4 *>(crow + col + 4 * j);
-                                float4 v = *p;
-                                v.x += __uint_as_float(r[4 * j + 0]);
-                                v.y += __uint_as_float(r[4 * j + 1]);
-                                v.z += __uint_as_float(r[4 * j + 2]);
-                                v.w += __uint_as_float(r[4 * j + 3]);
-                                *p = v;
-                            }
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col + j < N) crow[col + j] += __uint_as_float(r[j]);
-                    }
-                }
-            }
+            if (vec4)
+                epilogue_rows_vec4(t_row, crow, row, n0, M, N, c_next);
+            else
+                epilogue_rows_scalar(t_row, crow, row, n0, M, N);
             tc_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -268,6 +330,210 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 1) {
         tc_fence_after_sync();
         tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// =============================================================================
+// CTA-pair variant: clusters of 2, 256 x 256 tiles, cta_group::2.
+// =============================================================================
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_f16f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                            const __grid_constant__ CUtensorMap tmB, float *__restrict__ C, int M,
+                            int N, int K, long long ldc, int vec4) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // same offset in both CTAs
+
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + P_STAGES * A_BOX_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sB + P_STAGES * P_STAGE_B);
+    uint64_t *full = bars;                   // used in the even CTA only
+    uint64_t *empty = bars + P_STAGES;       // both CTAs
+    uint64_t *acc_full = bars + 2 * P_STAGES;  // both CTAs
+    uint64_t *acc_empty = acc_full + 2;      // even CTA only
+    uint64_t *drain = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const uint32_t warp = warp_id(), lane = lane_id();
+    const uint32_t rank = cluster_ctarank();  // 0 = even CTA (issues the MMAs)
+    const uint32_t peer = rank ^ 1u;
+    const int cluster = static_cast<int>(blockIdx.x >> 1);
+    const int num_clusters = static_cast<int>(gridDim.x >> 1);
+    const int num_m = (M + P_BM - 1) / P_BM;
+    const int num_n = (N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n;
+    const int num_kb = (K + BK - 1) / BK;
+    unsigned int *status = &g_wait_status;
+    const uint32_t peer_abort = mapa_shared(smem_u32(const_cast<int *>(abort_flag)), peer);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 8);  // the epilogue warps of both CTAs
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_map(&tmA);
+        tma_prefetch_map(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before_sync();
+    cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+
+    // A wait that gave up here also stops the peer CTA.
+    auto give_up = [&]() { st_shared_cluster_u32(peer_abort, 1u); };
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (lane == 0) {
+            const uint64_t policy = l2_policy_evict_normal();
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            for (int t = cluster; t < num_tiles && ok; t += num_clusters) {
+                int m_blk, n_blk;
+                tile_coords(t, num_m, num_n, P_GROUP_M, m_blk, n_blk);
+                const int m_pair = m_blk * P_BM, n_pair = n_blk * BN;
+                // Boxes entirely outside the tensor are not loaded (their
+                // accumulator rows / columns are never stored).
+                const int a_mine = (m_pair + 128 * static_cast<int>(rank) < M) ? 1 : 0;
+                const int a_even = 1, a_odd = (m_pair + 128 < M) ? 1 : 0;
+                const int n_mine = n_pair + 128 * static_cast<int>(rank);
+                auto boxes = [&](int n_start) { return max(0, min(2, (N - n_start + 63) / 64)); };
+                const int nb_mine = boxes(n_mine);
+                const uint32_t tx = static_cast<uint32_t>(a_even + a_odd) * A_BOX_BYTES +
+                                    static_cast<uint32_t>(boxes(n_pair) + boxes(n_pair + 128)) *
+                                        B_BOX_BYTES;
+                const int m_mine = m_pair + 128 * static_cast<int>(rank);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status,
+                                   kSiteProducerEmpty)) {
+                        give_up();
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full_even = mapa_shared(smem_u32(&full[stage]), 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], tx);
+                    const int k0 = kb * BK;
+                    if (a_mine)
+                        tma_load_2d_pair(sA + stage * A_BOX_BYTES, &tmA, full_even, k0, m_mine,
+                                         policy);
+                    for (int j = 0; j < nb_mine; ++j)
+                        tma_load_2d_pair(sB + stage * P_STAGE_B + j * B_BOX_BYTES, &tmB,
+                                         full_even, n_mine + 64 * j, k0, policy);
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // This CTA's copies complete on the even CTA's barriers, which
+                // only that CTA can wait on: give them time to land.
+                spin_ns(2000000);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (even CTA) ----------------
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(P_BM, BN, false, true);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true, issued_any = false;
+            for (int t = cluster; t < num_tiles && ok; t += num_clusters) {
+                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, status,
+                               kSiteMmaAccEmpty)) {
+                    give_up();
+                    ok = false;
+                    break;
+                }
+                tc_fence_after_sync();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, status, kSiteMmaFull)) {
+                        give_up();
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
+                    const uint32_t a_base = smem_u32(sA + stage * A_BOX_BYTES);
+                    const uint32_t b_base = smem_u32(sB + stage * P_STAGE_B);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                        const uint64_t b_desc =
+                            smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
+                        umma_f16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    issued_any = true;
+                    umma_commit_pair_multicast(&empty[stage], 0x3);
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair_multicast(&acc_full[acc], 0x3);
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            if (!ok && issued_any) {
+                umma_commit_pair_local(drain);
+                drain_wait(drain, 0, status);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+        const uint32_t q = warp & 3u;
+        uint32_t acc = 0, acc_phase = 0;
+        for (int t = cluster; t < num_tiles; t += num_clusters) {
+            int m_blk, n_blk;
+            tile_coords(t, num_m, num_n, P_GROUP_M, m_blk, n_blk);
+            const int m0 = m_blk * P_BM + 128 * static_cast<int>(rank), n0 = n_blk * BN;
+            const int row = m0 + static_cast<int>(q * 32 + lane);
+            float *crow = C + static_cast<long long>(row) * ldc;
+            float4 c_next[8];
+            if (vec4) load_c_chunk(c_next, crow, n0, N, row < M);
+            if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, status,
+                           kSiteEpilogueAccFull)) {
+                give_up();
+                break;
+            }
+            tc_fence_after_sync();
+            const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
+            if (vec4)
+                epilogue_rows_vec4(t_row, crow, row, n0, M, N, c_next);
+            else
+                epilogue_rows_scalar(t_row, crow, row, n0, M, N);
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+        __syncwarp();
+    }
+
+    // Neither CTA leaves (or frees TMEM) while the other may still touch its
+    // shared memory or TMEM: remote arrivals, peer copies and MMAs all precede
+    // this barrier.
+    tc_fence_before_sync();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after_sync();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
     }
 }
 
@@ -293,11 +559,14 @@ namespace {
 struct DeviceInfo {
     int sm_count = 0;
     int major = 0, minor = 0;
+    int max_pairs = 0;  // CTA pairs resident at once
+    unsigned int *status = nullptr;  // device address of g_wait_status
     bool attr_set = false;
 };
 
 std::mutex g_dev_mu;
 DeviceInfo g_dev[64];
+std::atomic<int> g_variant{0};  // 0 auto, 1 single CTA, 2 CTA pair
 
 int device_info(DeviceInfo **out) {
     int dev = 0;
@@ -318,8 +587,31 @@ int device_info(DeviceInfo **out) {
                          dev, d.major, d.minor);
     if (!d.attr_set) {
         e = cudaFuncSetAttribute(gemm::gemm_f16f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(gemm::SMEM_BYTES));
-        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute");
+                                 static_cast<int>(gemm::S_SMEM));
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(single)");
+        e = cudaFuncSetAttribute(gemm::gemm_f16f32_pair_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(gemm::P_SMEM));
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(pair)");
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2 * (d.sm_count / 2), 1, 1);
+        cfg.blockDim = dim3(gemm::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = gemm::P_SMEM;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        e = cudaOccupancyMaxActiveClusters(&clusters, gemm::gemm_f16f32_pair_kernel, &cfg);
+        if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveClusters");
+        d.max_pairs = clusters;
+        void *sym = nullptr;
+        e = cudaGetSymbolAddress(&sym, g_wait_status);
+        if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(g_wait_status)");
+        d.status = static_cast<unsigned int *>(sym);
         d.attr_set = true;
     }
     *out = &d;
@@ -362,11 +654,18 @@ int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_
     int rc = device_info(&dev);
     if (rc != CUDAIR_OK) return rc;
 
+    const int variant = g_variant.load();
+    if (variant == 3 || (variant == 0 && M <= 64))
+        return gemm_skinny_launch(a, b, c, static_cast<int>(M), static_cast<int>(N),
+                                  static_cast<int>(K), lda, ldb, ldc, dev->sm_count, dev->status,
+                                  stream);
+    const bool pair = (variant == 2) || (variant == 0 && M > 128 && dev->max_pairs > 0);
+
     alignas(64) CUtensorMap tmA, tmB;
     {
         const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
         const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
-        const uint32_t box[2] = {64, gemm::BM};
+        const uint32_t box[2] = {64, 128};
         rc = encode_tiled_internal(&tmA, CUDAIR_TENSOR_MAP_FLOAT16, 2,
                                    reinterpret_cast<uint64_t>(a), dims, strides, box, nullptr,
                                    CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B,
@@ -384,14 +683,35 @@ int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_
         if (rc != CUDAIR_OK) return rc;
     }
 
-    const int64_t tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
-    const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
     const int vec4 = ((reinterpret_cast<uintptr_t>(c) & 15u) == 0 && ldc % 4 == 0 && N % 4 == 0) ? 1 : 0;
-    gemm::gemm_f16f32_kernel<<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(
-        tmA, tmB, c, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
-        static_cast<long long>(ldc), vec4);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_error(e, "gemm_f16f32_kernel launch");
+    const int Mi = static_cast<int>(M), Ni = static_cast<int>(N), Ki = static_cast<int>(K);
+    const long long ldcl = static_cast<long long>(ldc);
+    cudaError_t e;
+    if (pair) {
+        const int64_t tiles = ((M + gemm::P_BM - 1) / gemm::P_BM) * ((N + gemm::BN - 1) / gemm::BN);
+        const int pairs = static_cast<int>(tiles < dev->max_pairs ? tiles : dev->max_pairs);
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2 * pairs, 1, 1);
+        cfg.blockDim = dim3(gemm::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = gemm::P_SMEM;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel, tmA, tmB, c, Mi, Ni, Ki, ldcl, vec4);
+        if (e != cudaSuccess) return cuda_error(e, "gemm_f16f32_pair_kernel launch");
+    } else {
+        const int64_t tiles = ((M + gemm::S_BM - 1) / gemm::S_BM) * ((N + gemm::BN - 1) / gemm::BN);
+        const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
+        gemm::gemm_f16f32_kernel<<<grid, gemm::THREADS, gemm::S_SMEM, stream>>>(tmA, tmB, c, Mi, Ni,
+                                                                                 Ki, ldcl, vec4);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_error(e, "gemm_f16f32_kernel launch");
+    }
     return CUDAIR_OK;
 }
 
@@ -415,6 +735,16 @@ CUDAIR_API int cudair_gemm_f16f32(const void *a, const void *b, float *c, int64_
     return gemm_f16f32_launch(a, b, c, M, N, K, lda, ldb, ldc, static_cast<cudaStream_t>(stream));
 }
 
+CUDAIR_API int cudair_set_gemm_variant(int variant) {
+    clear_error();
+    if (variant < 0 || variant > 3)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm variant %d, want 0 (auto), 1 (single CTA), 2 (CTA pair) or 3 (few rows)",
+                         variant);
+    g_variant.store(variant);
+    return CUDAIR_OK;
+}
+
 CUDAIR_API int cudair_wait_status(uint32_t *status, int clear) {
     clear_error();
     cudaError_t e = cudaDeviceSynchronize();
@@ -428,7 +758,10 @@ CUDAIR_API int cudair_wait_status(uint32_t *status, int clear) {
         e = cudaMemcpyToSymbol(g_wait_status, &zero, sizeof(zero));
         if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyToSymbol(g_wait_status)");
     }
-    if (v) return set_error(CUDAIR_ERR_TIMEOUT, "cudair: a bounded device wait gave up (status 0x%x)", v);
+    if (v) {
+        skinny_reset_workspace();
+        return set_error(CUDAIR_ERR_TIMEOUT, "cudair: a bounded device wait gave up (status 0x%x)", v);
+    }
     return CUDAIR_OK;
 }
 

@@ -1,0 +1,299 @@
+// module_demos.cuh - the remaining entry points of the reference's hopper and
+// vecadd example packages, with the reference's names and parameter ABI, so
+// the module is a drop-in for those packages' tests (TestHopper,
+// TestTensorMap, TestLaunchEx, the vecadd run program).
+//
+// Every wait on an mbarrier here is bounded (kDemoWaitNs); a wait that runs
+// out gives up and the kernel returns, leaving its outputs unwritten, which
+// the caller's check then reports.  None of these kernels traps.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace cudair_demo {
+
+constexpr int kBlock = 256;                     // the reference's blockSize (hopper.go:10)
+constexpr uint64_t kDemoWaitNs = 1000000000ull;  // 1 s
+
+__device__ __forceinline__ uint32_t s_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_parity(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(s_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded phase wait; false when it gave up.
+__device__ __forceinline__ bool mbar_wait_parity(uint64_t *bar, uint32_t parity) {
+    const uint64_t t0 = now_ns();
+    while (!mbar_try_wait_parity(bar, parity))
+        if (now_ns() - t0 > kDemoWaitNs) return false;
+    return true;
+}
+
+}  // namespace cudair_demo
+
+// ---- vecadd package: Saxpy, Square (examples/vecadd/vecadd.go:13-28) --------
+
+// y = alpha * x + y with a grid-stride loop (vecadd.go:13-18).  The product
+// and the sum are rounded separately (no fused multiply-add), as the
+// reference's CPU check computes them.
+extern "C" __global__ void Saxpy(float alpha, const float *__restrict__ x, float *__restrict__ y,
+                                 int n) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        y[i] = __fadd_rn(__fmul_rn(alpha, x[i]), y[i]);
+}
+
+// x[i] = x[i] * x[i] in place (vecadd.go:20-28).
+extern "C" __global__ void Square(float *__restrict__ x, int n) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        x[i] = __fmul_rn(x[i], x[i]);
+}
+
+// ---- hopper package (examples/hopper/hopper.go) ------------------------------
+
+// Clusters of two blocks: each block fills its shared tile with
+// block*1000 + tid and reads its partner's through distributed shared
+// memory; info[block] = rank + 10*size + 100*clusterID + 1000*numClusters
+// (hopper.go:16-35).  256 threads per block.
+extern "C" __global__ void __cluster_dims__(2, 1, 1) ClusterExchange(int *out, int *info) {
+    using namespace cudair_demo;
+    __shared__ int tile[kBlock];
+    const int tid = threadIdx.x, b = blockIdx.x;
+    if (tid < kBlock) tile[tid] = b * 1000 + tid;
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    uint32_t rank, size, cid, ncl;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(size));
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(cid));
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(ncl));
+    if (tid < kBlock) {
+        uint32_t remote;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(s_addr(&tile[tid])), "r"(rank ^ 1u));
+        int v;
+        asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
+        out[static_cast<int64_t>(b) * blockDim.x + tid] = v;
+    }
+    if (tid == 0) info[b] = static_cast<int>(rank + 10 * size + 100 * cid + 1000 * ncl);
+    // No block leaves while its partner may still read its tile.
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// mbarrier as a block barrier: every thread deposits in[i] in shared memory,
+// arrives, waits for the phase; thread 0 then sums the block
+// (hopper.go:42-64).
+extern "C" __global__ void MBarrierSum(const int *in, int *out) {
+    using namespace cudair_demo;
+    __shared__ uint64_t bar;
+    __shared__ int vals[kBlock];
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        mbar_init(&bar, blockDim.x);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid < kBlock) vals[tid] = in[static_cast<int64_t>(blockIdx.x) * blockDim.x + tid];
+    uint64_t token;
+    asm volatile("mbarrier.arrive.shared::cta.b64 %0, [%1];" : "=l"(token) : "r"(s_addr(&bar)) : "memory");
+    bool ok = false;
+    const uint64_t t0 = now_ns();
+    while (!ok && now_ns() - t0 <= kDemoWaitNs) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.test_wait.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(s_addr(&bar)), "l"(token)
+            : "memory");
+        ok = done != 0;
+    }
+    // Every thread has finished polling before the barrier is invalidated.
+    __syncthreads();
+    if (tid == 0 && ok) {
+        int s = 0;
+        for (int k = 0; k < kBlock; ++k) s += vals[k];
+        out[blockIdx.x] = s;
+        asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(s_addr(&bar)) : "memory");
+    }
+}
+
+// Bulk copies (TMA without a tensor map): each block copies its 1 KiB slice
+// of in to shared memory completing on an mbarrier, doubles it, and copies it
+// back to out with a bulk store (hopper.go:71-100).  n is a multiple of 256.
+extern "C" __global__ void TmaDouble(const int *in, int *out, int n) {
+    using namespace cudair_demo;
+    __shared__ __align__(128) int tile[kBlock];
+    __shared__ uint64_t bar;
+    const int tid = threadIdx.x;
+    const int base = blockIdx.x * kBlock;
+    if (base >= n) return;
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_addr(&bar)),
+                     "r"(static_cast<uint32_t>(kBlock * sizeof(int)))
+                     : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                s_addr(tile)),
+            "l"(in + base), "r"(static_cast<uint32_t>(kBlock * sizeof(int))), "r"(s_addr(&bar))
+            : "memory");
+    }
+    const bool landed = mbar_wait_parity(&bar, 0);
+    if (!landed) return;  // the copy's bytes are counted on `bar`; nothing else reads the tile
+    if (tid < kBlock) tile[tid] *= 2;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async proxy
+    __syncthreads();
+    if (tid == 0) {
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(out + base),
+                     "r"(s_addr(tile)), "r"(static_cast<uint32_t>(kBlock * sizeof(int)))
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+}
+
+// leader[i] = the lane elect.sync picks in the warp, elected[i] = 1 in that
+// lane only (hopper.go:104-115).
+extern "C" __global__ void Elect(int *leader, int *elected) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    uint32_t l, e;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\telect.sync r|p, 0xffffffff;\n\t"
+        "mov.u32 %0, r;\n\tselp.u32 %1, 1, 0, p;\n\t}"
+        : "=r"(l), "=r"(e));
+    leader[i] = static_cast<int>(l);
+    elected[i] = static_cast<int>(e);
+}
+
+// Programmatic dependent launch: wait for the prerequisite grid, write
+// out[i] = i, let dependents launch (hopper.go:119-127).
+extern "C" __global__ void GridDep(int *out) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    out[i] = i;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+
+// One 32 x 32 fp32 tile through two TMA tensor maps that live in global
+// memory: block (bx, by) loads the tile at (32 bx, 32 by), doubles it in
+// shared memory and stores it at the same coordinates of the second tensor;
+// edges follow the maps' out-of-bounds rules (hopper.go:136-176).
+extern "C" __global__ void TensorTileDouble(const CUtensorMap *src, const CUtensorMap *dst) {
+    using namespace cudair_demo;
+    constexpr int kTile = 32;
+    __shared__ __align__(128) float t[kTile * kTile];
+    __shared__ uint64_t bar;
+    const int tid = threadIdx.x;
+    const int x0 = blockIdx.x * kTile, y0 = blockIdx.y * kTile;  // x0 * 4 B: 16-byte aligned
+    __shared__ int landed;
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_addr(&bar)),
+                     "r"(static_cast<uint32_t>(sizeof(t)))
+                     : "memory");
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%2, %3}], [%4];" ::"r"(s_addr(t)),
+            "l"(reinterpret_cast<uint64_t>(src)), "r"(x0), "r"(y0), "r"(s_addr(&bar))
+            : "memory");
+        landed = mbar_wait_parity(&bar, 0) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!landed) return;
+    for (int i = tid; i < kTile * kTile; i += blockDim.x) t[i] *= 2.0f;
+    __syncthreads();
+    if (tid == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                         reinterpret_cast<uint64_t>(dst)),
+                     "r"(x0), "r"(y0), "r"(s_addr(t))
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+}
+
+// The cluster shape comes only from the launch attribute (no
+// __cluster_dims__): block b writes its rank + 100 * cluster size
+// (hopper.go:178-187).
+extern "C" __global__ void ClusterRankRuntime(int *out) {
+    if (threadIdx.x != 0) return;
+    uint32_t rank, size;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(size));
+    out[blockIdx.x] = static_cast<int>(rank + 100 * size);
+}
+
+// ldmatrix / stmatrix round trips on four 8x8 fp16 matrices (hopper.go:230-275):
+// out[0:256] after stmatrix.x4 (the tile unchanged), out[256:512] after
+// stmatrix.x4.trans (each matrix transposed), out[512:640] after
+// stmatrix.x2.trans of the first two, out[640:704] after x1.trans of the first.
+extern "C" __global__ void StMatrixRoundTrip(const __half *in, __half *out) {
+    __shared__ __align__(16) __half t[4 * 64];
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x >= 32) return;
+    for (int i = lane; i < 4 * 64; i += 32) t[i] = in[i];
+    __syncwarp();
+    const uint32_t row = cudair_demo::s_addr(&t[lane * 8]);
+    uint32_t v4[4], v2[2], v1;
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v4[0]), "=r"(v4[1]), "=r"(v4[2]), "=r"(v4[3]) : "r"(row));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(v2[0]), "=r"(v2[1]) : "r"(row));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x1.shared.b16 {%0}, [%1];" : "=r"(v1) : "r"(row));
+    __syncwarp();
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(row), "r"(v4[0]),
+                 "r"(v4[1]), "r"(v4[2]), "r"(v4[3])
+                 : "memory");
+    __syncwarp();
+    for (int i = lane; i < 4 * 64; i += 32) out[i] = t[i];
+    __syncwarp();
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(row),
+                 "r"(v4[0]), "r"(v4[1]), "r"(v4[2]), "r"(v4[3])
+                 : "memory");
+    __syncwarp();
+    for (int i = lane; i < 4 * 64; i += 32) out[4 * 64 + i] = t[i];
+    __syncwarp();
+    asm volatile("stmatrix.sync.aligned.m8n8.x2.trans.shared.b16 [%0], {%1, %2};" ::"r"(row), "r"(v2[0]),
+                 "r"(v2[1])
+                 : "memory");
+    __syncwarp();
+    for (int i = lane; i < 2 * 64; i += 32) out[8 * 64 + i] = t[i];
+    __syncwarp();
+    asm volatile("stmatrix.sync.aligned.m8n8.x1.trans.shared.b16 [%0], {%1};" ::"r"(row), "r"(v1) : "memory");
+    __syncwarp();
+    for (int i = lane; i < 64; i += 32) out[10 * 64 + i] = t[i];
+}

@@ -58,6 +58,11 @@ def gemm(a, b, c, stream=None) -> None:
                                    a.stride(0), b.stride(0), c.stride(0), _stream(stream)))
 
 
+def set_gemm_variant(variant: int) -> None:
+    """0 = automatic, 1 = single-CTA 128x256 tiles, 2 = CTA-pair 256x256 tiles."""
+    check(lib().cudair_set_gemm_variant(variant))
+
+
 def vecadd(a, b, out, stream=None) -> None:
     """out = a + b over fp32 vectors (VecAdd's operands)."""
     import torch

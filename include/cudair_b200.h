@@ -155,6 +155,20 @@ int cudair_gemm_f16f32(const void *a, const void *b, float *c,
                        int64_t lda, int64_t ldb, int64_t ldc, void *stream);
 
 /*
+ * Selects the GEMM kernel variant for subsequent calls in this process:
+ * 0 = automatic (few-row kernel when M <= 64, CTA pairs with 256 x 256 tiles
+ * when M > 128, single CTAs with 128 x 256 tiles in between), 1 = single CTA,
+ * 2 = CTA pair, 3 = few-row kernel (M <= 64 only).  All variants compute the
+ * same result within fp32 rounding; the choice only affects speed.
+ *
+ * The few-row kernel (B as the MMA's 128-row side, K split evenly over all
+ * SMs) keeps its partial sums in a 16 MB per-device workspace that the
+ * library allocates on its first use on a device; its calls on one device
+ * must not overlap in time (issue them on one stream).
+ */
+int cudair_set_gemm_variant(int variant);
+
+/*
  * out[i] = a[i] + b[i] for i < n (fp32, round-to-nearest: bit-exact with a
  * CPU add).  Same operands as VecAdd (vecadd.go:6); the launcher sizes a
  * persistent grid over the SMs.  Any alignment is accepted.  Asynchronous.

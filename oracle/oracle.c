@@ -307,6 +307,24 @@ EXPORT void oracle_vecadd(const float *a, const float *b, float *out,
     par_for(n, threads, 1 << 16, add_range, &c);
 }
 
+/* ---- Saxpy / Square CPU models (examples/vecadd/run/main.go:62-76) ------- */
+
+/* y[i] = alpha * x[i] + y[i], product and sum rounded separately. */
+EXPORT void oracle_saxpy(float alpha, const float *x, float *y, int64_t n)
+{
+    for (int64_t i = 0; i < n; i++) {
+        float p = alpha * x[i];
+        y[i] = p + y[i];
+    }
+}
+
+/* x[i] = x[i] * x[i]. */
+EXPORT void oracle_square(float *x, int64_t n)
+{
+    for (int64_t i = 0; i < n; i++)
+        x[i] = x[i] * x[i];
+}
+
 /* ---- ReduceF32 CPU model ----------------------------------------------- */
 
 /* Go's math.Min / math.Max on float64 (-Inf/+Inf win, then NaN, -0 < +0). */

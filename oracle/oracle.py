@@ -9,6 +9,7 @@ Each function names the reference test whose CPU model oracle.c restates:
   matmul16/gemm   the i-j-k float32 loop, advanced_test.go:466-475
   vecadd          out = a + b, main_test.go:51
   reduce_f32      math.Min/Max fold per warp, advanced_test.go:572-579
+  saxpy/square    examples/vecadd/run/main.go:62-76
 """
 from __future__ import annotations
 
@@ -55,6 +56,8 @@ def lib():
         L.oracle_matmul16.argtypes = [_f32p, _f32p, _f32p, _f32p, ctypes.c_int32]
         L.oracle_vecadd.argtypes = [_f32p, _f32p, _f32p, _i64, ctypes.c_int]
         L.oracle_reduce_f32.argtypes = [_f32p, _f32p, ctypes.c_int32]
+        L.oracle_saxpy.argtypes = [ctypes.c_float, _f32p, _f32p, _i64]
+        L.oracle_square.argtypes = [_f32p, _i64]
         L.oracle_stream_word.restype = ctypes.c_uint64
         L.oracle_stream_word.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
         L.oracle_fill_uniform.argtypes = [_f32p, _i64, ctypes.c_uint64, _i64,
@@ -149,6 +152,22 @@ def vecadd(a, b, threads=1) -> np.ndarray:
     b = np.ascontiguousarray(b, dtype=np.float32)
     out = np.empty_like(a)
     lib().oracle_vecadd(_p(a, _f32p), _p(b, _f32p), _p(out, _f32p), a.size, threads)
+    return out
+
+
+def saxpy(alpha: float, x, y) -> np.ndarray:
+    """alpha*x + y, rounded after the product and after the sum
+    (the check of examples/vecadd/run/main.go:62-68)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.array(y, dtype=np.float32, copy=True)
+    lib().oracle_saxpy(alpha, _p(x, _f32p), _p(out, _f32p), x.size)
+    return out
+
+
+def square(x) -> np.ndarray:
+    """x*x (the check of examples/vecadd/run/main.go:70-76)."""
+    out = np.array(x, dtype=np.float32, copy=True)
+    lib().oracle_square(_p(out, _f32p), out.size)
     return out
 
 

@@ -33,6 +33,22 @@ def no_wait_timeouts(dev, cudair):
     assert kernels.wait_status(clear=True) == 0
 
 
+@pytest.fixture(params=[1, 2, 3], ids=["single", "pair", "fewrows"])
+def variant(request, dev, cudair):
+    """Runs a test on each GEMM kernel in turn: single CTA (128x256 tiles),
+    CTA pair (256x256) and the few-row kernel (M <= 64), then restores the
+    automatic choice."""
+    from cudair import kernels
+    kernels.set_gemm_variant(request.param)
+    yield request.param
+    kernels.set_gemm_variant(0)
+
+
+def _applies(variant, M):
+    if variant == 3 and M > 64:
+        pytest.skip("the few-row kernel takes M <= 64")
+
+
 def kat(M, N, K):
     """The TestHopper generator (advanced_test.go:459-463) on an M x K / K x N
     grid: af = (i+2j)%7-3, bf = (3i+j)%5-2, c = j-i."""
@@ -98,9 +114,10 @@ def test_matmul16_reference_launch_seeded_n256(dev, module, oracle, golden_dir):
 
 
 @pytest.mark.parametrize("n", [64, 256, 512, 1024, 2048])
-def test_matmul16_tcgen05_kat_exact(dev, cudair, n):
+def test_matmul16_tcgen05_kat_exact(dev, cudair, variant, n):
     import torch
     from cudair import kernels
+    _applies(variant, n)
     af, bf, c, want = kat(n, n, n)
     da, db, dc = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16), _dev(c, dev, torch.float32)
     kernels.matmul16(da, db, dc)
@@ -132,11 +149,13 @@ def test_matmul16_tcgen05_seeded_n256(dev, cudair, oracle, golden_dir):
 
 @pytest.mark.parametrize("M,N,K", [
     (1, 8, 8), (7, 16, 24), (128, 256, 64), (129, 264, 72), (200, 264, 136), (300, 1000, 1000),
-    (513, 8, 4096), (16, 14336, 512), (1000, 2056, 520),
+    (513, 8, 4096), (16, 14336, 512), (1000, 2056, 520), (257, 136, 64), (384, 384, 8),
+    (5, 136, 200), (33, 1000, 1000), (64, 2048, 8), (48, 520, 4104), (17, 128, 64),
 ])
-def test_gemm_tcgen05_ragged_kat_exact(dev, cudair, M, N, K):
+def test_gemm_tcgen05_ragged_kat_exact(dev, cudair, variant, M, N, K):
     import torch
     from cudair import kernels
+    _applies(variant, M)
     af, bf, c, want = kat(M, N, K)
     da, db, dc = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16), _dev(c, dev, torch.float32)
     kernels.gemm(da, db, dc)
@@ -145,11 +164,13 @@ def test_gemm_tcgen05_ragged_kat_exact(dev, cudair, M, N, K):
     assert bad.size == 0, f"{len(bad)} mismatches, first at {tuple(bad[0])}"
 
 
-def test_gemm_tcgen05_padded_leading_dims(dev, cudair):
+@pytest.mark.parametrize("M", [300, 40])
+def test_gemm_tcgen05_padded_leading_dims(dev, cudair, variant, M):
     # lda, ldb, ldc larger than the logical widths; untouched padding.
     import torch
     from cudair import kernels
-    M, N, K = 300, 520, 200
+    _applies(variant, M)
+    N, K = 520, 200
     af, bf, c, want = kat(M, N, K)
     A = torch.zeros(M, K + 24, dtype=torch.float16, device=dev)
     B = torch.zeros(K, N + 8, dtype=torch.float16, device=dev)
@@ -168,11 +189,12 @@ def _seeded_normal_f16(oracle, n, seed, std):
     return h, oracle.f16_to_f32(h)
 
 
-def test_gemm_8192_cube_seeded(dev, cudair, oracle):
+def test_gemm_8192_cube_seeded(dev, cudair, oracle, variant):
     # The 8192^3 configuration: A, B ~ fp16(N(0,1)/sqrt(8192)), C ~ N(0,1).
     import torch
     from cudair import kernels
     n = 8192
+    _applies(variant, n)
     a16, af = _seeded_normal_f16(oracle, n * n, 6, 1.0 / np.sqrt(n))
     b16, bf = _seeded_normal_f16(oracle, n * n, 7, 1.0 / np.sqrt(n))
     c = oracle.normal(n * n, 8).reshape(n, n)
@@ -216,14 +238,39 @@ def test_gemm_skinny_decode_shape(dev, cudair, oracle):
     assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
 
 
-def test_gemm_repeated_calls_accumulate(dev, cudair):
+@pytest.mark.parametrize("M", [256, 16])
+def test_gemm_repeated_calls_accumulate(dev, cudair, variant, M):
     # C = A.B + C is not idempotent: two calls add the product twice.
     import torch
     from cudair import kernels
-    M, N, K = 256, 512, 320
+    _applies(variant, M)
+    N, K = 512, 320
     af, bf, c, want1 = kat(M, N, K)
     da, db, dc = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16), _dev(c, dev, torch.float32)
     kernels.gemm(da, db, dc)
     kernels.gemm(da, db, dc)
     want2 = want1 + (want1 - c)
     assert np.array_equal(dc.cpu().numpy(), want2)
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 14336, 4096), (3, 4096, 12288), (64, 1024, 520)])
+def test_fewrows_deterministic_and_within_tolerance(dev, cudair, oracle, M, N, K):
+    # The split-K fix-up sums partials in a fixed order: two runs from the
+    # same C give identical bits, and both match the oracle within tolerance.
+    import torch
+    from cudair import kernels
+    a16, af = _seeded_normal_f16(oracle, M * K, 61, 1.0)
+    b16, bf = _seeded_normal_f16(oracle, K * N, 62, 0.02)
+    c = oracle.uniform(M * N, 63).reshape(M, N)
+    da = torch.from_numpy(a16.view(np.int16)).to(dev).view(torch.float16).reshape(M, K)
+    db = torch.from_numpy(b16.view(np.int16)).to(dev).view(torch.float16).reshape(K, N)
+    outs = []
+    for _ in range(2):
+        dc = torch.from_numpy(c.copy()).to(dev)
+        kernels.gemm(da, db, dc)
+        outs.append(dc.cpu().numpy())
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    want = oracle.gemm_ikj(af.reshape(M, K), bf.reshape(K, N), c)
+    tol_rel, tol_max = oracle.gemm_tolerance(K, np.abs(af).max(), np.abs(bf).max())
+    rel, mx, bad = oracle.error_norms(outs[0], want)
+    assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
