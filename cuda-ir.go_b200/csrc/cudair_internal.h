@@ -63,6 +63,8 @@ int encode_tiled_internal(CUtensorMap *out, uint32_t data_type, uint32_t rank,
                           uint32_t l2_promotion, uint32_t oob_fill);
 
 int sm_count_current_device(int *count);
+// Device address of the bounded-wait status word on the current device.
+int wait_status_current_device(unsigned int **status);
 
 int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int K, int64_t lda,
                        int64_t ldb, int64_t ldc, int sm_count, unsigned int *status,

@@ -396,3 +396,157 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
 }
 
 }  // namespace cudair
+
+// =============================================================================
+// The same few-row GEMM for callers that cannot allocate device memory.
+//
+// Some hosts must not allocate device memory themselves: their device memory
+// is owned end to end by another allocator (a framework's caching allocator,
+// or a pool reserved at start-up), or allocation is forbidden once they are
+// serving, because cudaMalloc may synchronise the device and stall every
+// other stream.  cudair_gemm_f16f32 allocates the few-row kernel's 16 MB
+// workspace on its first call on a device; this entry point instead keeps
+// that scratch space in a fixed array in the library's own device memory,
+// reserved when the library is loaded, so no call ever allocates.
+// =============================================================================
+
+namespace cudair {
+namespace {
+// Tile counters for up to 4096 n-tiles (N <= 524288), then 4 MiB of partial
+// sums: 4 MiB + 16 KiB in all.
+constexpr int kNoAllocMaxTiles = 4096;
+constexpr size_t kNoAllocCounterBytes = kNoAllocMaxTiles * sizeof(unsigned int);
+constexpr size_t kNoAllocPartialBytes = 4u << 20;
+}  // namespace
+}  // namespace cudair
+
+// The scratch array.  It is part of the library's device image, so every GPU
+// that loads the library holds it until the process exits.
+static __device__ __align__(256) unsigned char
+    g_noalloc_scratch[cudair::kNoAllocCounterBytes + cudair::kNoAllocPartialBytes];
+
+namespace cudair {
+namespace {
+
+// Host code cannot use g_noalloc_scratch as a pointer: on the host the name
+// only stands in for the device variable.  The device address is looked up
+// once per device, with that device current, and cached.
+std::mutex g_noalloc_mu;
+unsigned char *g_noalloc_ptr[64];
+bool g_noalloc_attr[64];
+
+int noalloc_scratch(unsigned char **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: device index %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+        g_noalloc_ptr[dev] = static_cast<unsigned char *>(p);
+    }
+    if (!g_noalloc_attr[dev]) {
+        e = cudaFuncSetAttribute(skinny::gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(skinny::SMEM_BYTES));
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(skinny)");
+        g_noalloc_attr[dev] = true;
+    }
+    *out = g_noalloc_ptr[dev];
+    return CUDAIR_OK;
+}
+
+}  // namespace
+}  // namespace cudair
+
+// C (M x N) += A (M x K) . B (K x N) for 1 <= M <= 64 and N <= 524288, with
+// the same operands, layout rules and results as cudair_gemm_f16f32 (up to
+// fp32 rounding order), without allocating.  The first call on a device looks
+// up the scratch array's address and sets the kernel's shared-memory limit;
+// make that first call before any stream capture.  Each call clears the tile
+// counters it uses (cudaMemsetAsync on `stream`) and then launches; all calls
+// share the one array, so calls that overlap on the GPU (e.g. on different
+// streams at once) race and must be avoided.  With M > 16 the kernel runs on
+// fewer CTAs so that the partial sums fit the array.
+CUDAIR_API int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c, int64_t M,
+                                          int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                                          int64_t ldc, void *stream) {
+    using namespace cudair;
+    clear_error();
+    if (M < 0 || N < 0 || K < 0)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_noalloc: negative size M=%lld N=%lld K=%lld",
+                         (long long)M, (long long)N, (long long)K);
+    if (M == 0 || N == 0 || K == 0) return CUDAIR_OK;  // C = C
+    if (M > skinny::MAX_M)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm_noalloc: M = %lld exceeds the maximum of %d rows", (long long)M,
+                         skinny::MAX_M);
+    if (N > static_cast<int64_t>(kNoAllocMaxTiles) * skinny::BN_T)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm_noalloc: N = %lld exceeds the maximum of %d columns", (long long)N,
+                         kNoAllocMaxTiles * skinny::BN_T);
+    if (K > INT32_MAX)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_noalloc: K must fit int32");
+    if (!a || !b || !c) return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_noalloc: nil pointer");
+    if (lda < K || ldb < N || ldc < N)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm_noalloc: leading dimensions lda=%lld ldb=%lld ldc=%lld too small",
+                         (long long)lda, (long long)ldb, (long long)ldc);
+    if (lda % 8 || ldb % 8)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm_noalloc: lda=%lld and ldb=%lld must be multiples of 8",
+                         (long long)lda, (long long)ldb);
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_noalloc: A and B must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(c) & 3u)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_noalloc: C must be 4-byte aligned");
+
+    int sms = 0;
+    int rc = sm_count_current_device(&sms);
+    if (rc != CUDAIR_OK) return rc;
+    unsigned int *status = nullptr;
+    if ((rc = wait_status_current_device(&status)) != CUDAIR_OK) return rc;
+    unsigned char *scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch)) != CUDAIR_OK) return rc;
+
+    const int Mi = static_cast<int>(M), Ni = static_cast<int>(N), Ki = static_cast<int>(K);
+    const int mpad = (Mi + 15) / 16 * 16;
+    alignas(64) CUtensorMap tmB, tmA;
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+        const uint32_t box[2] = {64, skinny::BK};
+        rc = encode_tiled_internal(&tmB, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(b),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+        const uint32_t box[2] = {skinny::BK, static_cast<uint32_t>(mpad)};
+        rc = encode_tiled_internal(&tmA, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(a),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    const int n_tiles = (Ni + skinny::BN_T - 1) / skinny::BN_T;
+    const long long T = static_cast<long long>(n_tiles) * ((Ki + skinny::BK - 1) / skinny::BK);
+    const long long slot_pair = 2LL * skinny::BN_T * mpad * static_cast<long long>(sizeof(float));
+    long long grid = T < sms ? T : sms;
+    const long long fit = static_cast<long long>(kNoAllocPartialBytes) / slot_pair;
+    if (grid > fit) grid = fit;
+
+    unsigned int *counters = reinterpret_cast<unsigned int *>(scratch);
+    float *partials = reinterpret_cast<float *>(scratch + kNoAllocCounterBytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(counters, 0, static_cast<size_t>(n_tiles) * sizeof(unsigned int), s);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMemsetAsync(no-alloc tile counters)");
+    skinny::gemm_skinny_kernel<<<static_cast<unsigned>(grid), skinny::THREADS, skinny::SMEM_BYTES, s>>>(
+        tmB, tmA, c, Mi, Ni, Ki, static_cast<long long>(ldc), mpad, counters, partials, status);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch (no-alloc)");
+    return CUDAIR_OK;
+}

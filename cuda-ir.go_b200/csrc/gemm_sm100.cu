@@ -620,6 +620,14 @@ int device_info(DeviceInfo **out) {
 
 }  // namespace
 
+int wait_status_current_device(unsigned int **status) {
+    DeviceInfo *d = nullptr;
+    int rc = device_info(&d);
+    if (rc != CUDAIR_OK) return rc;
+    *status = d->status;
+    return CUDAIR_OK;
+}
+
 int sm_count_current_device(int *count) {
     DeviceInfo *d = nullptr;
     int rc = device_info(&d);

@@ -169,6 +169,25 @@ int cudair_gemm_f16f32(const void *a, const void *b, float *c,
 int cudair_set_gemm_variant(int variant);
 
 /*
+ * The few-row GEMM (1 <= M <= 64, N <= 524288) without any device
+ * allocation.  No counterpart in the reference: it serves hosts that must not
+ * allocate device memory themselves, because another allocator owns all of
+ * it (a framework's caching allocator, a pool reserved at start-up) or
+ * because allocating after start-up is forbidden (cudaMalloc may synchronise
+ * the device and stall other streams).  Operands, layout rules and results
+ * are those of cudair_gemm_f16f32 (up to fp32 rounding order).  Its scratch
+ * space is a fixed 4 MiB + 16 KiB array in the library's device image, held
+ * on every GPU that loads the library until exit; sizes beyond the maximum
+ * return CUDAIR_ERR_INVALID.  The first call on a device looks up the array's
+ * address and sets the kernel's shared-memory limit (make it before any stream
+ * capture); every call clears the tile counters it uses and then launches.
+ * All calls share the array: calls that overlap on the GPU race.
+ */
+int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c,
+                               int64_t M, int64_t N, int64_t K,
+                               int64_t lda, int64_t ldb, int64_t ldc, void *stream);
+
+/*
  * out[i] = a[i] + b[i] for i < n (fp32, round-to-nearest: bit-exact with a
  * CPU add).  Same operands as VecAdd (vecadd.go:6); the launcher sizes a
  * persistent grid over the SMs.  Any alignment is accepted.  Asynchronous.
