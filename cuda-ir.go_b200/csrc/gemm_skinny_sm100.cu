@@ -50,14 +50,6 @@ static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 // Workspace layout: tile counters first, then two partial slots per CTA.
 constexpr size_t COUNTER_BYTES = 256 * 1024;  // 65536 n-tiles
 constexpr int MAX_TILES = COUNTER_BYTES / 4;
-constexpr size_t partial_bytes(int grid, int mpad) {
-    return static_cast<size_t>(grid) * 2 * BN_T * mpad * 4;
-}
-
-struct Range {
-    long long start, end;  // [start, end) in k-block units
-};
-
 __device__ __forceinline__ long long range_start(int c, long long T, int G) {
     return (static_cast<long long>(c) * T) / G;
 }
@@ -268,17 +260,30 @@ __global__ void __launch_bounds__(THREADS, 1)
             named_bar_sync(1, 128);
             if (*last_flag) {
                 __threadfence();
+                // Sixteen rows at a time: C and then each contributor's
+                // partials are loaded as independent batches (one memory
+                // latency per contributor, not per element) and added in
+                // contributor order.
                 if (n < N) {
-                    for (int m = 0; m < M; ++m) {
-                        float *p = C + static_cast<long long>(m) * ldc + n;
-                        float v = *p;
+                    for (int m0 = 0; m0 < M; m0 += 16) {
+                        float v[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            v[i] = (m0 + i < M) ? C[static_cast<long long>(m0 + i) * ldc + n] : 0.f;
                         for (int cc = c_lo; cc <= c_hi; ++cc) {
                             const long long s_cc = range_start(cc, T, G);
                             const int sl = (s_cc / num_kb == t) ? 0 : 1;
                             const float *pc = partials + (static_cast<size_t>(cc) * 2 + sl) * BN_T * mpad;
-                            v += __ldcg(pc + m * BN_T + nl);
+                            float pv[16];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                pv[i] = (m0 + i < M) ? __ldcg(pc + (m0 + i) * BN_T + nl) : 0.f;
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) v[i] += pv[i];
                         }
-                        *p = v;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            if (m0 + i < M) C[static_cast<long long>(m0 + i) * ldc + n] = v[i];
                     }
                 }
                 if (leader) counters[t] = 0u;

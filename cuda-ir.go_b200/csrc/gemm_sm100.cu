@@ -94,26 +94,49 @@ __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity, unsig
     mbar_wait(bar, parity, &never, status, kSiteDrain);
 }
 
+// C is read once and written once per launch: its accesses skip L1 and are
+// marked first to leave L2, so the stream of C does not push out the A and B
+// panels that other tiles re-read.
+__device__ __forceinline__ uint64_t c_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ float4 ld_c(const float *p, uint64_t pol) {
+    float4 v;
+    asm volatile("ld.global.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
+}
+
+__device__ __forceinline__ void st_c(float *p, float4 v, uint64_t pol) {
+    asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "l"(pol)
+                 : "memory");
+}
+
 // 32 columns of C for this thread's row, as eight 16-byte loads.
 __device__ __forceinline__ void load_c_chunk(float4 (&v)[8], const float *crow, int col, int N,
-                                             bool row_ok) {
+                                             bool row_ok, uint64_t pol) {
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-        v[j] = (row_ok && col + 4 * j < N) ? *reinterpret_cast<const float4 *>(crow + col + 4 * j)
+        v[j] = (row_ok && col + 4 * j < N) ? ld_c(crow + col + 4 * j, pol)
                                            : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // Adds this warp's 32 accumulator rows (TMEM lanes from t_row, 256 columns)
 // to C and stores the sums.  c_next holds chunk 0 of C, loaded by the caller.
 __device__ __forceinline__ void epilogue_rows_vec4(uint32_t t_row, float *crow, int row, int n0,
-                                                   int M, int N, float4 (&c_next)[8]) {
+                                                   int M, int N, float4 (&c_next)[8], uint64_t pol) {
     const bool row_ok = row < M;
 #pragma unroll
     for (int ch = 0; ch < BN / 32; ++ch) {
         float4 c_cur[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) c_cur[j] = c_next[j];
-        if (ch + 1 < BN / 32) load_c_chunk(c_next, crow, n0 + (ch + 1) * 32, N, row_ok);
+        if (ch + 1 < BN / 32) load_c_chunk(c_next, crow, n0 + (ch + 1) * 32, N, row_ok, pol);
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + ch * 32, r);
         tmem_ld_wait();
@@ -127,7 +150,7 @@ __device__ __forceinline__ void epilogue_rows_vec4(uint32_t t_row, float *crow, 
                     v.y += __uint_as_float(r[4 * j + 1]);
                     v.z += __uint_as_float(r[4 * j + 2]);
                     v.w += __uint_as_float(r[4 * j + 3]);
-                    *reinterpret_cast<float4 *>(crow + col + 4 * j) = v;
+                    st_c(crow + col + 4 * j, v, pol);
                 }
             }
         }
@@ -299,6 +322,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const uint32_t q = warp & 3u;  // the TMEM lane quarter this warp may read
+        const uint64_t cpol = c_policy();
         uint32_t acc = 0, acc_phase = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int m_blk, n_blk;
@@ -307,13 +331,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int row = m0 + static_cast<int>(q * 32 + lane);
             float *crow = C + static_cast<long long>(row) * ldc;
             float4 c_next[8];
-            if (vec4) load_c_chunk(c_next, crow, n0, N, row < M);
+            if (vec4) load_c_chunk(c_next, crow, n0, N, row < M, cpol);
             if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull))
                 break;
             tc_fence_after_sync();
             const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
             if (vec4)
-                epilogue_rows_vec4(t_row, crow, row, n0, M, N, c_next);
+                epilogue_rows_vec4(t_row, crow, row, n0, M, N, c_next, cpol);
             else
                 epilogue_rows_scalar(t_row, crow, row, n0, M, N);
             tc_fence_before_sync();
@@ -496,6 +520,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
         // ---------------- epilogue (warps 2..5, both CTAs) ----------------
         const uint32_t q = warp & 3u;
+        const uint64_t cpol = c_policy();
         uint32_t acc = 0, acc_phase = 0;
         for (int t = cluster; t < num_tiles; t += num_clusters) {
             int m_blk, n_blk;
@@ -504,7 +529,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int row = m0 + static_cast<int>(q * 32 + lane);
             float *crow = C + static_cast<long long>(row) * ldc;
             float4 c_next[8];
-            if (vec4) load_c_chunk(c_next, crow, n0, N, row < M);
+            if (vec4) load_c_chunk(c_next, crow, n0, N, row < M, cpol);
             if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, status,
                            kSiteEpilogueAccFull)) {
                 give_up();
@@ -513,7 +538,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after_sync();
             const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
             if (vec4)
-                epilogue_rows_vec4(t_row, crow, row, n0, M, N, c_next);
+                epilogue_rows_vec4(t_row, crow, row, n0, M, N, c_next, cpol);
             else
                 epilogue_rows_scalar(t_row, crow, row, n0, M, N);
             tc_fence_before_sync();

@@ -297,3 +297,179 @@ extern "C" __global__ void StMatrixRoundTrip(const __half *in, __half *out) {
     __syncwarp();
     for (int i = lane; i < 64; i += 32) out[10 * 64 + i] = t[i];
 }
+
+// ---- tensor package: mma.sync m16n8k16 matmuls (examples/tensor/tensor.go:9-100) ----
+//
+// The reference's launch contract for these is one warp per 16 x 8 tile of
+// C (LaunchConfig1D((n/16)*(n/8)*32, 128)), a shape tcgen05 cannot take (its
+// smallest MMA has 64 rows and is issued for a whole CTA), so they keep the
+// warp-level m16n8k16 instruction.  Fragments are read straight from global
+// memory: lane l holds rows g = l/4 and g+8, columns 2t, 2t+1 (+8) of A
+// (t = l%4), k-rows 2t, 2t+1 (+8) of column g of B, and rows g, g+8, columns
+// 2t, 2t+1 of C.
+
+namespace cudair_tensor {
+
+__device__ __forceinline__ uint32_t pack2(uint16_t lo, uint16_t hi) {
+    return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+struct Tile {
+    int row, col;  // 16-row block, 8-column block
+    bool ok;
+};
+
+__device__ __forceinline__ Tile tile_of_warp(int n) {
+    const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int warp = static_cast<int>(gid / 32);
+    const int tiles = n / 8;
+    Tile t;
+    t.row = warp / tiles;
+    t.col = warp % tiles;
+    t.ok = t.row < n / 16;
+    return t;
+}
+
+// A fragment of the 16 x 16 tile at p (row-major, leading dimension n).
+__device__ __forceinline__ void frag_a(uint32_t (&a)[4], const uint16_t *p, int n) {
+    const int l = threadIdx.x & 31, g = l >> 2, t = l & 3;
+    a[0] = *reinterpret_cast<const uint32_t *>(p + g * n + 2 * t);
+    a[1] = *reinterpret_cast<const uint32_t *>(p + (g + 8) * n + 2 * t);
+    a[2] = *reinterpret_cast<const uint32_t *>(p + g * n + 2 * t + 8);
+    a[3] = *reinterpret_cast<const uint32_t *>(p + (g + 8) * n + 2 * t + 8);
+}
+
+// B fragment of the 16 x 8 tile at p, B row-major (k-rows, leading dimension n).
+__device__ __forceinline__ void frag_b_rows(uint32_t (&b)[2], const uint16_t *p, int n) {
+    const int l = threadIdx.x & 31, g = l >> 2, t = l & 3;
+    b[0] = pack2(p[(2 * t) * n + g], p[(2 * t + 1) * n + g]);
+    b[1] = pack2(p[(2 * t + 8) * n + g], p[(2 * t + 9) * n + g]);
+}
+
+// B fragment read column-major: element (k, j) at p[j * n + k].
+__device__ __forceinline__ void frag_b_cols(uint32_t (&b)[2], const uint16_t *p, int n) {
+    const int l = threadIdx.x & 31, g = l >> 2, t = l & 3;
+    b[0] = *reinterpret_cast<const uint32_t *>(p + g * n + 2 * t);
+    b[1] = *reinterpret_cast<const uint32_t *>(p + g * n + 2 * t + 8);
+}
+
+__device__ __forceinline__ void mma_f16_f32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ void mma_bf16_f32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ void mma_f16_f16(uint32_t (&d)[2], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f16.f16.f16.f16 {%0, %1}, {%2, %3, %4, %5}, {%6, %7}, {%0, %1};"
+        : "+r"(d[0]), "+r"(d[1])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ void load_acc(float (&d)[4], const float *p, int n) {
+    const int l = threadIdx.x & 31, g = l >> 2, t = l & 3;
+    d[0] = p[g * n + 2 * t];
+    d[1] = p[g * n + 2 * t + 1];
+    d[2] = p[(g + 8) * n + 2 * t];
+    d[3] = p[(g + 8) * n + 2 * t + 1];
+}
+
+__device__ __forceinline__ void store_acc(float *p, int n, const float (&d)[4]) {
+    const int l = threadIdx.x & 31, g = l >> 2, t = l & 3;
+    p[g * n + 2 * t] = d[0];
+    p[g * n + 2 * t + 1] = d[1];
+    p[(g + 8) * n + 2 * t] = d[2];
+    p[(g + 8) * n + 2 * t + 1] = d[3];
+}
+
+}  // namespace cudair_tensor
+
+// C = A.B, fp16 inputs, fp32 accumulate (tensor.go:15-29).
+extern "C" __global__ void MmaF16(const uint16_t *a, const uint16_t *b, float *c, int n) {
+    using namespace cudair_tensor;
+    const Tile tl = tile_of_warp(n);
+    if (!tl.ok) return;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < n; k += 16) {
+        uint32_t fa[4], fb[2];
+        frag_a(fa, a + static_cast<int64_t>(tl.row) * 16 * n + k, n);
+        frag_b_rows(fb, b + static_cast<int64_t>(k) * n + tl.col * 8, n);
+        mma_f16_f32(acc, fa, fb);
+    }
+    store_acc(c + static_cast<int64_t>(tl.row) * 16 * n + tl.col * 8, n, acc);
+}
+
+// C = A.B + Bias, the accumulator loaded from bias (tensor.go:31-47).
+extern "C" __global__ void MmaF16Bias(const uint16_t *a, const uint16_t *b, const float *bias, float *c,
+                                      int n) {
+    using namespace cudair_tensor;
+    const Tile tl = tile_of_warp(n);
+    if (!tl.ok) return;
+    float acc[4];
+    load_acc(acc, bias + static_cast<int64_t>(tl.row) * 16 * n + tl.col * 8, n);
+    for (int k = 0; k < n; k += 16) {
+        uint32_t fa[4], fb[2];
+        frag_a(fa, a + static_cast<int64_t>(tl.row) * 16 * n + k, n);
+        frag_b_rows(fb, b + static_cast<int64_t>(k) * n + tl.col * 8, n);
+        mma_f16_f32(acc, fa, fb);
+    }
+    store_acc(c + static_cast<int64_t>(tl.row) * 16 * n + tl.col * 8, n, acc);
+}
+
+// C = A.Bt^T with bt row-major, so B is read column-major (tensor.go:49-64).
+extern "C" __global__ void MmaF16Trans(const uint16_t *a, const uint16_t *bt, float *c, int n) {
+    using namespace cudair_tensor;
+    const Tile tl = tile_of_warp(n);
+    if (!tl.ok) return;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < n; k += 16) {
+        uint32_t fa[4], fb[2];
+        frag_a(fa, a + static_cast<int64_t>(tl.row) * 16 * n + k, n);
+        frag_b_cols(fb, bt + static_cast<int64_t>(tl.col) * 8 * n + k, n);
+        mma_f16_f32(acc, fa, fb);
+    }
+    store_acc(c + static_cast<int64_t>(tl.row) * 16 * n + tl.col * 8, n, acc);
+}
+
+// C = A.B accumulating in fp16 (tensor.go:66-81).
+extern "C" __global__ void MmaF16Half(const uint16_t *a, const uint16_t *b, uint16_t *c, int n) {
+    using namespace cudair_tensor;
+    const Tile tl = tile_of_warp(n);
+    if (!tl.ok) return;
+    uint32_t acc[2] = {0u, 0u};
+    for (int k = 0; k < n; k += 16) {
+        uint32_t fa[4], fb[2];
+        frag_a(fa, a + static_cast<int64_t>(tl.row) * 16 * n + k, n);
+        frag_b_rows(fb, b + static_cast<int64_t>(k) * n + tl.col * 8, n);
+        mma_f16_f16(acc, fa, fb);
+    }
+    const int l = threadIdx.x & 31, g = l >> 2, t = l & 3;
+    uint16_t *p = c + static_cast<int64_t>(tl.row) * 16 * n + tl.col * 8;
+    *reinterpret_cast<uint32_t *>(p + g * n + 2 * t) = acc[0];
+    *reinterpret_cast<uint32_t *>(p + (g + 8) * n + 2 * t) = acc[1];
+}
+
+// C = A.B with bfloat16 inputs (tensor.go:83-98).
+extern "C" __global__ void MmaBF16(const uint16_t *a, const uint16_t *b, float *c, int n) {
+    using namespace cudair_tensor;
+    const Tile tl = tile_of_warp(n);
+    if (!tl.ok) return;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < n; k += 16) {
+        uint32_t fa[4], fb[2];
+        frag_a(fa, a + static_cast<int64_t>(tl.row) * 16 * n + k, n);
+        frag_b_rows(fb, b + static_cast<int64_t>(k) * n + tl.col * 8, n);
+        mma_bf16_f32(acc, fa, fb);
+    }
+    store_acc(c + static_cast<int64_t>(tl.row) * 16 * n + tl.col * 8, n, acc);
+}

@@ -128,9 +128,13 @@ def ArgValue(v) -> Arg:
 
 
 def ArgBuffer(t) -> Arg:
-    """Passes a device buffer's pointer (ArgBuffer[T]); t is a torch tensor or an int."""
+    """Passes a device buffer's pointer (ArgBuffer[T]); t is a torch tensor or an int.
+    The argument keeps the tensor alive, so a temporary buffer is not freed (and its
+    memory handed to another allocation) before the launch that reads it."""
     ptr = t if isinstance(t, int) else t.data_ptr()
-    return Arg(bytes(ctypes.c_uint64(ptr)))
+    a = Arg(bytes(ctypes.c_uint64(ptr)))
+    a.buffer = None if isinstance(t, int) else t
+    return a
 
 
 def ArgBytes(p: bytes) -> Arg:

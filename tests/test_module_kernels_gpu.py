@@ -7,6 +7,8 @@ launched the way the reference's tests do, with the same known answers:
   TestLaunchEx (hostapi_test.go:360-466): RuntimeClusterDims,
       ProgrammaticDependentLaunch, Cooperative
   examples/vecadd/run/main.go:62-76: Saxpy, Square
+  TestTensor (tensor_test.go:23-145): MmaF16, MmaF16Bias, MmaF16Trans,
+      MmaF16Half, MmaBF16
 """
 import ctypes
 
@@ -62,7 +64,8 @@ def test_mbarrier_sum(dev, mod):
     from cudair import host
     x = (np.arange(BLOCKS * BS) % 7).astype(np.int32)
     dout = up(dev, np.zeros(BLOCKS, np.int32))
-    launch(mod, "MBarrierSum", cfg1d(BLOCKS * BS, BS), host.ArgBuffer(up(dev, x)), host.ArgBuffer(dout))
+    din = up(dev, x)
+    launch(mod, "MBarrierSum", cfg1d(BLOCKS * BS, BS), host.ArgBuffer(din), host.ArgBuffer(dout))
     assert np.array_equal(dout.cpu().numpy(), x.reshape(BLOCKS, BS).sum(axis=1).astype(np.int32))
 
 
@@ -70,7 +73,8 @@ def test_tma_double(dev, mod):
     from cudair import host
     x = (np.arange(BLOCKS * BS) * 3 - 100).astype(np.int32)
     dout = up(dev, np.zeros(BLOCKS * BS, np.int32))
-    launch(mod, "TmaDouble", cfg1d(BLOCKS * BS, BS), host.ArgBuffer(up(dev, x)), host.ArgBuffer(dout),
+    din = up(dev, x)
+    launch(mod, "TmaDouble", cfg1d(BLOCKS * BS, BS), host.ArgBuffer(din), host.ArgBuffer(dout),
            host.ArgValue(ctypes.c_int32(BLOCKS * BS)))
     assert np.array_equal(dout.cpu().numpy(), 2 * x)
 
@@ -97,7 +101,8 @@ def test_stmatrix_round_trip(dev, mod, oracle):
     from cudair import host
     inp = oracle.f32_to_f16(np.arange(1, 4 * 64 + 1, dtype=np.float32))
     dout = up(dev, np.zeros(11 * 64, np.uint16).view(np.int16))
-    launch(mod, "StMatrixRoundTrip", cfg1d(32, 32), host.ArgBuffer(up(dev, inp.view(np.int16))),
+    din = up(dev, inp.view(np.int16))
+    launch(mod, "StMatrixRoundTrip", cfg1d(32, 32), host.ArgBuffer(din),
            host.ArgBuffer(dout))
     out = dout.cpu().numpy().view(np.uint16)
     assert np.array_equal(out[:256], inp)
@@ -212,3 +217,74 @@ def test_saxpy_unfused_on_awkward_alpha(dev, mod, oracle):
     launch(mod, "Saxpy", cfg1d(n, 256), host.ArgValue(ctypes.c_float(alpha)), host.ArgBuffer(dx),
            host.ArgBuffer(dy), host.ArgValue(ctypes.c_int32(n)))
     assert np.array_equal(dy.cpu().numpy(), oracle.saxpy(float(alpha), x, y))
+
+
+# ---- TestTensor: the mma.sync m16n8k16 family (tensor_test.go:23-145) -----------
+
+def _elem(n, wi, wj, wij, m):
+    i = np.arange(n).reshape(n, 1)
+    j = np.arange(n).reshape(1, n)
+    return (wi * i + wj * j + wij * i * j) % m
+
+
+def _bf16_bits(x):
+    # small integers: bfloat16 holds them exactly, the top half of the f32 bits
+    return (np.asarray(x, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+
+@pytest.fixture(scope="module")
+def tensor_kat():
+    n = 64
+    af = (_elem(n, 7, 13, 3, 5) - 2).astype(np.float32)
+    bf = (_elem(n, 11, 5, 7, 5) - 2).astype(np.float32)
+    bias = (_elem(n, 3, 7, 5, 11) - 5).astype(np.float32)
+    want = (af.astype(np.int64) @ bf.astype(np.int64)).astype(np.float32)
+    return n, af, bf, bias, want
+
+
+def _mma_cfg(n):
+    return cfg1d((n // 16) * (n // 8) * 32, 128)
+
+
+def test_mma_f16_family(dev, mod, oracle, tensor_kat):
+    from cudair import host
+    n, af, bf, bias, want = tensor_kat
+    ah = up(dev, oracle.f32_to_f16(af).view(np.int16))
+    bh = up(dev, oracle.f32_to_f16(bf).view(np.int16))
+    bth = up(dev, oracle.f32_to_f16(np.ascontiguousarray(bf.T)).view(np.int16))
+    n32 = host.ArgValue(ctypes.c_int32(n))
+    dc = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "MmaF16", _mma_cfg(n), host.ArgBuffer(ah), host.ArgBuffer(bh), host.ArgBuffer(dc), n32)
+    assert np.array_equal(dc.cpu().numpy(), want)
+    dc2 = up(dev, np.zeros((n, n), np.float32))
+    dbias = up(dev, bias)
+    launch(mod, "MmaF16Bias", _mma_cfg(n), host.ArgBuffer(ah), host.ArgBuffer(bh),
+           host.ArgBuffer(dbias), host.ArgBuffer(dc2), n32)
+    assert np.array_equal(dc2.cpu().numpy(), want + bias)
+    dc3 = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "MmaF16Trans", _mma_cfg(n), host.ArgBuffer(ah), host.ArgBuffer(bth), host.ArgBuffer(dc3), n32)
+    assert np.array_equal(dc3.cpu().numpy(), want)
+
+
+def test_mma_f16_half_accumulator(dev, mod, oracle, tensor_kat):
+    from cudair import host
+    n, af, bf, _, want = tensor_kat
+    dc = up(dev, np.zeros((n, n), np.int16))
+    ah = up(dev, oracle.f32_to_f16(af).view(np.int16))
+    bh = up(dev, oracle.f32_to_f16(bf).view(np.int16))
+    launch(mod, "MmaF16Half", _mma_cfg(n), host.ArgBuffer(ah), host.ArgBuffer(bh), host.ArgBuffer(dc),
+           host.ArgValue(ctypes.c_int32(n)))
+    # |want| <= 256, so the fp16 accumulator is exact too
+    got = oracle.f16_to_f32(dc.cpu().numpy().view(np.uint16))
+    assert np.array_equal(got, want)
+
+
+def test_mma_bf16(dev, mod, tensor_kat):
+    from cudair import host
+    n, af, bf, _, want = tensor_kat
+    dc = up(dev, np.zeros((n, n), np.float32))
+    ab = up(dev, _bf16_bits(af).view(np.int16))
+    bb = up(dev, _bf16_bits(bf).view(np.int16))
+    launch(mod, "MmaBF16", _mma_cfg(n), host.ArgBuffer(ab), host.ArgBuffer(bb), host.ArgBuffer(dc),
+           host.ArgValue(ctypes.c_int32(n)))
+    assert np.array_equal(dc.cpu().numpy(), want)
