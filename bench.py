@@ -406,6 +406,7 @@ def run_ours(args, world, rank, local):
     from cudair import kernels
 
     dev = torch.device("cuda", local)
+    kernels.set_gemm_variant(args.gemm_variant)
     peaks, peak_kind = load_peaks()
     traffic = load_traffic()
     g = torch.Generator(device=dev)
@@ -504,6 +505,8 @@ def main():
     ap.add_argument("--gather", action="store_true", help="also all-gather C over NCCL (timed apart)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds for the CPU baseline")
+    ap.add_argument("--gemm-variant", type=int, default=0,
+                    help="GEMM kernel choice (cudair_set_gemm_variant; 0 = automatic)")
     ap.add_argument("--workload", choices=["all", "gemm", "vecadd", "skinny"], default="all",
                     help="run one part only (for profiling); the JSON line needs 'all'")
     args = ap.parse_args()

@@ -38,6 +38,7 @@ struct Driver {
     CUresult (*cuModuleUnload)(CUmodule);
     CUresult (*cuModuleGetFunction)(CUfunction *, CUmodule, const char *);
     CUresult (*cuLaunchKernelEx)(const CUlaunchConfig *, CUfunction, void **, void **);
+    CUresult (*cuMemGetAddressRange)(CUdeviceptr *, size_t *, CUdeviceptr);
     CUresult (*cuTensorMapEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                        const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                        const cuuint32_t *, CUtensorMapInterleave,

@@ -87,6 +87,7 @@ void open_driver() {
         bind(h, g_drv.cuModuleUnload, "cuModuleUnload") &&
         bind(h, g_drv.cuModuleGetFunction, "cuModuleGetFunction") &&
         bind(h, g_drv.cuLaunchKernelEx, "cuLaunchKernelEx") &&
+        bind(h, g_drv.cuMemGetAddressRange, "cuMemGetAddressRange_v2") &&
         bind(h, g_drv.cuTensorMapEncodeTiled, "cuTensorMapEncodeTiled");
     if (g_drv_rc == CUDAIR_OK) {
         CUresult r = g_drv.cuInit(0);

@@ -10,6 +10,9 @@
 //     Each CTA loads its own 128 rows of A and its own 128 columns of B (no
 //     multicast), so a CTA moves 32 KB per 64-wide k-block instead of 48 KB;
 //     seven 32 KB stages fit in shared memory.  The even CTA issues the MMAs.
+//   pair, wide: the same with 256 x 512 tiles (two N = 256 MMAs per k-step
+//     into one accumulator that fills TMEM; each CTA loads 48 KB per k-block
+//     for twice the FLOPs, a four-stage ring).
 //   single (M <= 128): one CTA per SM computes 128 x 256 tiles with
 //     tcgen05.mma.cta_group::1 from a four-stage ring of 48 KB stages.
 //
@@ -67,14 +70,28 @@ constexpr int S_GROUP_M = 16;
 constexpr uint32_t S_STAGE_B = BN / 64 * B_BOX_BYTES;  // 32 KB
 constexpr size_t S_SMEM = 1024 + S_STAGES * (A_BOX_BYTES + S_STAGE_B) + BAR_BYTES;
 
-// CTA-pair variant
+// CTA-pair variants: NB 256-column MMA blocks per tile (NB = 1: 256 x 256
+// tiles, two accumulators; NB = 2: 256 x 512 tiles, one accumulator filling
+// TMEM, a quarter fewer operand bytes per FLOP).
 constexpr int P_BM = 256;  // rows per pair tile, 128 per CTA
-constexpr int P_STAGES = 7;
 constexpr int P_GROUP_M = 8;
-constexpr uint32_t P_STAGE_B = BN / 2 / 64 * B_BOX_BYTES;  // 16 KB: this CTA's 128 columns
-constexpr size_t P_SMEM = 1024 + P_STAGES * (A_BOX_BYTES + P_STAGE_B) + BAR_BYTES;
+// The CTA-pair tile the automatic choice uses (1: 256 x 256, 2: 256 x 512).
+#ifndef CUDAIR_AUTO_PAIR_NB
+#define CUDAIR_AUTO_PAIR_NB 1
+#endif
+template <int NB>
+struct PairCfg {
+    static constexpr int TILE_N = 256 * NB;
+    static constexpr uint32_t STAGE_B = NB * 2 * B_BOX_BYTES;  // this CTA's 128 x NB columns
+    static constexpr uint32_t STAGE = A_BOX_BYTES + STAGE_B;
+    static constexpr int STAGES_FIT = static_cast<int>((227 * 1024 - 1024 - BAR_BYTES) / STAGE);
+    static constexpr int STAGES = STAGES_FIT < 7 ? STAGES_FIT : 7;
+    static constexpr int ACCS = 2 / NB;  // accumulator buffers in 512 TMEM columns
+    static constexpr size_t SMEM = 1024 + STAGES * STAGE + BAR_BYTES;
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
 
-static_assert(S_SMEM <= 227 * 1024 && P_SMEM <= 227 * 1024, "shared memory budget");
+static_assert(S_SMEM <= 227 * 1024, "shared memory budget");
 
 // Row-block / column-block of persistent tile index t (grouped raster).
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int &m_blk,
@@ -358,23 +375,26 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // =============================================================================
-// CTA-pair variant: clusters of 2, 256 x 256 tiles, cta_group::2.
+// CTA-pair variants: clusters of 2, 256 x (256 NB) tiles, cta_group::2.
 // =============================================================================
+template <int NB>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmB, float *__restrict__ C, int M,
                             int N, int K, long long ldc, int vec4) {
+    using Cfg = PairCfg<NB>;
+    constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // same offset in both CTAs
 
     uint8_t *sA = smem;
-    uint8_t *sB = smem + P_STAGES * A_BOX_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sB + P_STAGES * P_STAGE_B);
-    uint64_t *full = bars;                   // used in the even CTA only
-    uint64_t *empty = bars + P_STAGES;       // both CTAs
-    uint64_t *acc_full = bars + 2 * P_STAGES;  // both CTAs
-    uint64_t *acc_empty = acc_full + 2;      // even CTA only
+    uint8_t *sB = smem + STAGES * A_BOX_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * Cfg::STAGE_B);
+    uint64_t *full = bars;                     // used in the even CTA only
+    uint64_t *empty = bars + STAGES;           // both CTAs
+    uint64_t *acc_full = bars + 2 * STAGES;    // both CTAs
+    uint64_t *acc_empty = acc_full + 2;        // even CTA only
     uint64_t *drain = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -385,14 +405,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int cluster = static_cast<int>(blockIdx.x >> 1);
     const int num_clusters = static_cast<int>(gridDim.x >> 1);
     const int num_m = (M + P_BM - 1) / P_BM;
-    const int num_n = (N + BN - 1) / BN;
+    const int num_n = (N + Cfg::TILE_N - 1) / Cfg::TILE_N;
     const int num_tiles = num_m * num_n;
     const int num_kb = (K + BK - 1) / BK;
     unsigned int *status = &g_wait_status;
     const uint32_t peer_abort = mapa_shared(smem_u32(const_cast<int *>(abort_flag)), peer);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < P_STAGES; ++s) {
+        for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -417,6 +437,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     // A wait that gave up here also stops the peer CTA.
     auto give_up = [&]() { st_shared_cluster_u32(peer_abort, 1u); };
+    // 64-column B boxes that start inside the tensor, among the 128 columns from n.
+    auto boxes = [&](int n) { return max(0, min(2, (N - n + 63) / 64)); };
 
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
@@ -427,18 +449,18 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int t = cluster; t < num_tiles && ok; t += num_clusters) {
                 int m_blk, n_blk;
                 tile_coords(t, num_m, num_n, P_GROUP_M, m_blk, n_blk);
-                const int m_pair = m_blk * P_BM, n_pair = n_blk * BN;
-                // Boxes entirely outside the tensor are not loaded (their
-                // accumulator rows / columns are never stored).
-                const int a_mine = (m_pair + 128 * static_cast<int>(rank) < M) ? 1 : 0;
-                const int a_even = 1, a_odd = (m_pair + 128 < M) ? 1 : 0;
-                const int n_mine = n_pair + 128 * static_cast<int>(rank);
-                auto boxes = [&](int n_start) { return max(0, min(2, (N - n_start + 63) / 64)); };
-                const int nb_mine = boxes(n_mine);
-                const uint32_t tx = static_cast<uint32_t>(a_even + a_odd) * A_BOX_BYTES +
-                                    static_cast<uint32_t>(boxes(n_pair) + boxes(n_pair + 128)) *
-                                        B_BOX_BYTES;
+                const int m_pair = m_blk * P_BM, n_pair = n_blk * Cfg::TILE_N;
+                // Block h of this CTA holds columns n_pair + 256 h + 128 rank + [0, 128):
+                // MMA h takes its first 128 columns from the even CTA, the next 128
+                // from the odd one.  Boxes and rows entirely outside the tensor are
+                // not loaded (their accumulator rows / columns are never stored).
                 const int m_mine = m_pair + 128 * static_cast<int>(rank);
+                const int a_mine = (m_mine < M) ? 1 : 0;
+                const int a_odd = (m_pair + 128 < M) ? 1 : 0;
+                uint32_t tx = static_cast<uint32_t>(1 + a_odd) * A_BOX_BYTES;
+                for (int h = 0; h < NB; ++h)
+                    tx += static_cast<uint32_t>(boxes(n_pair + 256 * h) + boxes(n_pair + 256 * h + 128)) *
+                          B_BOX_BYTES;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status,
                                    kSiteProducerEmpty)) {
@@ -452,10 +474,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (a_mine)
                         tma_load_2d_pair(sA + stage * A_BOX_BYTES, &tmA, full_even, k0, m_mine,
                                          policy);
-                    for (int j = 0; j < nb_mine; ++j)
-                        tma_load_2d_pair(sB + stage * P_STAGE_B + j * B_BOX_BYTES, &tmB,
-                                         full_even, n_mine + 64 * j, k0, policy);
-                    if (++stage == P_STAGES) {
+#pragma unroll
+                    for (int h = 0; h < NB; ++h) {
+                        const int n_mine = n_pair + 256 * h + 128 * static_cast<int>(rank);
+                        const int nb_mine = boxes(n_mine);
+                        for (int j = 0; j < nb_mine; ++j)
+                            tma_load_2d_pair(sB + stage * Cfg::STAGE_B + (2 * h + j) * B_BOX_BYTES,
+                                             &tmB, full_even, n_mine + 64 * j, k0, policy);
+                    }
+                    if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -471,7 +498,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (even CTA) ----------------
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(P_BM, BN, false, true);
+            constexpr uint32_t idesc = idesc_f16_f32(P_BM, 256, false, true);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true, issued_any = false;
             for (int t = cluster; t < num_tiles && ok; t += num_clusters) {
@@ -482,7 +509,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     break;
                 }
                 tc_fence_after_sync();
-                const uint32_t d_tmem = tmem_base + acc * BN;
+                const uint32_t d_tmem = tmem_base + acc * 256;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, status, kSiteMmaFull)) {
                         give_up();
@@ -491,24 +518,28 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     tc_fence_after_sync();
                     const uint32_t a_base = smem_u32(sA + stage * A_BOX_BYTES);
-                    const uint32_t b_base = smem_u32(sB + stage * P_STAGE_B);
+                    const uint32_t b_base = smem_u32(sB + stage * Cfg::STAGE_B);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
-                        const uint64_t b_desc =
-                            smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
-                        umma_f16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+#pragma unroll
+                        for (int h = 0; h < NB; ++h) {
+                            const uint64_t b_desc = smem_desc_sw128(
+                                b_base + h * 2 * B_BOX_BYTES + kk * 2048, B_BOX_BYTES, 1024);
+                            umma_f16_ss_pair(d_tmem + h * 256, a_desc, b_desc, idesc,
+                                             (kb | kk) != 0 ? 1u : 0u);
+                        }
                     }
                     issued_any = true;
                     umma_commit_pair_multicast(&empty[stage], 0x3);
-                    if (++stage == P_STAGES) {
+                    if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
                 umma_commit_pair_multicast(&acc_full[acc], 0x3);
-                acc ^= 1u;
+                if (Cfg::ACCS == 2) acc ^= 1u;
                 if (acc == 0) acc_phase ^= 1u;
             }
             if (!ok && issued_any) {
@@ -525,7 +556,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int t = cluster; t < num_tiles; t += num_clusters) {
             int m_blk, n_blk;
             tile_coords(t, num_m, num_n, P_GROUP_M, m_blk, n_blk);
-            const int m0 = m_blk * P_BM + 128 * static_cast<int>(rank), n0 = n_blk * BN;
+            const int m0 = m_blk * P_BM + 128 * static_cast<int>(rank), n0 = n_blk * Cfg::TILE_N;
             const int row = m0 + static_cast<int>(q * 32 + lane);
             float *crow = C + static_cast<long long>(row) * ldc;
             float4 c_next[8];
@@ -536,15 +567,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                 break;
             }
             tc_fence_after_sync();
-            const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
-            if (vec4)
-                epilogue_rows_vec4(t_row, crow, row, n0, M, N, c_next, cpol);
-            else
-                epilogue_rows_scalar(t_row, crow, row, n0, M, N);
+            const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * 256;
+#pragma unroll 1
+            for (int h = 0; h < NB; ++h) {
+                if (vec4) {
+                    if (h > 0) load_c_chunk(c_next, crow, n0 + 256 * h, N, row < M, cpol);
+                    epilogue_rows_vec4(t_row + 256 * h, crow, row, n0 + 256 * h, M, N, c_next, cpol);
+                } else {
+                    epilogue_rows_scalar(t_row + 256 * h, crow, row, n0 + 256 * h, M, N);
+                }
+            }
             tc_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
-            acc ^= 1u;
+            if (Cfg::ACCS == 2) acc ^= 1u;
             if (acc == 0) acc_phase ^= 1u;
         }
         __syncwarp();
@@ -614,10 +650,14 @@ int device_info(DeviceInfo **out) {
         e = cudaFuncSetAttribute(gemm::gemm_f16f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(gemm::S_SMEM));
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(single)");
-        e = cudaFuncSetAttribute(gemm::gemm_f16f32_pair_kernel,
+        e = cudaFuncSetAttribute(gemm::gemm_f16f32_pair_kernel<1>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(gemm::P_SMEM));
+                                 static_cast<int>(gemm::PairCfg<1>::SMEM));
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(pair)");
+        e = cudaFuncSetAttribute(gemm::gemm_f16f32_pair_kernel<2>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(gemm::PairCfg<2>::SMEM));
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(pair, wide)");
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -626,11 +666,11 @@ int device_info(DeviceInfo **out) {
         attr[0].val.clusterDim.z = 1;
         cfg.gridDim = dim3(2 * (d.sm_count / 2), 1, 1);
         cfg.blockDim = dim3(gemm::THREADS, 1, 1);
-        cfg.dynamicSmemBytes = gemm::P_SMEM;
+        cfg.dynamicSmemBytes = gemm::PairCfg<1>::SMEM;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         int clusters = 0;
-        e = cudaOccupancyMaxActiveClusters(&clusters, gemm::gemm_f16f32_pair_kernel, &cfg);
+        e = cudaOccupancyMaxActiveClusters(&clusters, gemm::gemm_f16f32_pair_kernel<1>, &cfg);
         if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveClusters");
         d.max_pairs = clusters;
         void *sym = nullptr;
@@ -692,8 +732,10 @@ int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_
         return gemm_skinny_launch(a, b, c, static_cast<int>(M), static_cast<int>(N),
                                   static_cast<int>(K), lda, ldb, ldc, dev->sm_count, dev->status,
                                   stream);
-    const bool pair = (variant == 2) || (variant == 0 && M > 128 && dev->max_pairs > 0);
-
+    // 0 auto, 1 single CTA, 2 CTA pair (256 x 256), 4 CTA pair (256 x 512).
+    const bool pair_auto = variant == 0 && M > 128 && dev->max_pairs > 0;
+    const int pair_nb = (variant == 4) ? 2 : ((variant == 2 || pair_auto) ? CUDAIR_AUTO_PAIR_NB : 0);
+    const bool pair = pair_nb > 0;
     alignas(64) CUtensorMap tmA, tmB;
     {
         const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
@@ -721,7 +763,8 @@ int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_
     const long long ldcl = static_cast<long long>(ldc);
     cudaError_t e;
     if (pair) {
-        const int64_t tiles = ((M + gemm::P_BM - 1) / gemm::P_BM) * ((N + gemm::BN - 1) / gemm::BN);
+        const int tile_n = 256 * pair_nb;
+        const int64_t tiles = ((M + gemm::P_BM - 1) / gemm::P_BM) * ((N + tile_n - 1) / tile_n);
         const int pairs = static_cast<int>(tiles < dev->max_pairs ? tiles : dev->max_pairs);
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
@@ -731,11 +774,16 @@ int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_
         attr[0].val.clusterDim.z = 1;
         cfg.gridDim = dim3(2 * pairs, 1, 1);
         cfg.blockDim = dim3(gemm::THREADS, 1, 1);
-        cfg.dynamicSmemBytes = gemm::P_SMEM;
         cfg.stream = stream;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel, tmA, tmB, c, Mi, Ni, Ki, ldcl, vec4);
+        if (pair_nb == 2) {
+            cfg.dynamicSmemBytes = gemm::PairCfg<2>::SMEM;
+            e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<2>, tmA, tmB, c, Mi, Ni, Ki, ldcl, vec4);
+        } else {
+            cfg.dynamicSmemBytes = gemm::PairCfg<1>::SMEM;
+            e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<1>, tmA, tmB, c, Mi, Ni, Ki, ldcl, vec4);
+        }
         if (e != cudaSuccess) return cuda_error(e, "gemm_f16f32_pair_kernel launch");
     } else {
         const int64_t tiles = ((M + gemm::S_BM - 1) / gemm::S_BM) * ((N + gemm::BN - 1) / gemm::BN);
@@ -770,9 +818,10 @@ CUDAIR_API int cudair_gemm_f16f32(const void *a, const void *b, float *c, int64_
 
 CUDAIR_API int cudair_set_gemm_variant(int variant) {
     clear_error();
-    if (variant < 0 || variant > 3)
+    if (variant < 0 || variant > 4)
         return set_error(CUDAIR_ERR_INVALID,
-                         "cudair: gemm variant %d, want 0 (auto), 1 (single CTA), 2 (CTA pair) or 3 (few rows)",
+                         "cudair: gemm variant %d, want 0 (auto), 1 (single CTA), 2 (CTA pair), "
+                         "3 (few rows) or 4 (CTA pair, 256 x 512 tiles)",
                          variant);
     g_variant.store(variant);
     return CUDAIR_OK;

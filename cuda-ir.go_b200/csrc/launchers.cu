@@ -52,14 +52,27 @@ CUDAIR_API int cudair_reduce_f32(const float *in, float *out, int32_t n, void *s
 
 // ---- B replication for the row-sharded GEMM -----------------------------------
 
-CUDAIR_API int cudair_ipc_export(const void *dev_ptr, void *handle_out) {
+CUDAIR_API int cudair_ipc_export(const void *dev_ptr, void *handle_out, uint64_t *offset_out) {
     clear_error();
-    if (!dev_ptr || !handle_out) return set_error(CUDAIR_ERR_INVALID, "cudair: ipc_export: nil pointer");
+    if (!dev_ptr || !handle_out || !offset_out)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: ipc_export: nil pointer");
     static_assert(sizeof(cudaIpcMemHandle_t) == CUDAIR_IPC_HANDLE_BYTES, "IPC handle size");
+    // The handle names the whole allocation that holds dev_ptr (a caching
+    // allocator hands out pieces of larger blocks), and the importer maps
+    // that allocation's base: report where dev_ptr sits inside it.
+    const Driver *d = nullptr;
+    int rc = load_driver(&d);
+    if (rc != CUDAIR_OK) return rc;
+    if ((rc = ensure_context()) != CUDAIR_OK) return rc;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    CUresult r = d->cuMemGetAddressRange(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr));
+    if (r != CUDA_SUCCESS) return cu_error(r, "cuMemGetAddressRange");
     cudaIpcMemHandle_t h;
-    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr));
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
     if (e != cudaSuccess) return cuda_error(e, "cudaIpcGetMemHandle");
     memcpy(handle_out, &h, sizeof(h));
+    *offset_out = static_cast<uint64_t>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
     return CUDAIR_OK;
 }
 

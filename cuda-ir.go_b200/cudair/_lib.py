@@ -43,7 +43,7 @@ SIGNATURES = {
     "cudair_reduce_f32": (c_int, [c_vp, c_vp, ctypes.c_int32, c_vp]),
     "cudair_wait_status": (c_int, [_u32p, c_int]),
     "cudair_wait_timeout_selftest": (c_int, [c_u64, c_vp]),
-    "cudair_ipc_export": (c_int, [c_vp, c_vp]),
+    "cudair_ipc_export": (c_int, [c_vp, c_vp, _u64p]),
     "cudair_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
     "cudair_ipc_close": (c_int, [c_vp]),
     "cudair_peer_copy": (c_int, [c_vp, c_vp, c_size, c_vp]),

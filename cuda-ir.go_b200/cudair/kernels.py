@@ -59,7 +59,8 @@ def gemm(a, b, c, stream=None) -> None:
 
 
 def set_gemm_variant(variant: int) -> None:
-    """0 = automatic, 1 = single-CTA 128x256 tiles, 2 = CTA-pair 256x256 tiles."""
+    """0 = automatic, 1 = single-CTA 128x256 tiles, 2 = CTA-pair 256x256 tiles,
+    3 = few-row kernel (M <= 64), 4 = CTA-pair 256x512 tiles."""
     check(lib().cudair_set_gemm_variant(variant))
 
 

@@ -72,8 +72,11 @@ def replicate_from_rank0(buf, rank: int, world: int,
     if rank == 0:
         if copy_fn is None:
             h = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
-            _lib.check(_lib.lib().cudair_ipc_export(ctypes.c_void_p(buf.data_ptr()), h))
-            handle = bytes(h)
+            off = ctypes.c_uint64()
+            _lib.check(_lib.lib().cudair_ipc_export(ctypes.c_void_p(buf.data_ptr()), h,
+                                                    ctypes.byref(off)))
+            # The handle maps the whole allocation; the offset locates buf in it.
+            handle = bytes(h) + off.value.to_bytes(8, "little")
         else:
             handle = copy_fn("export", buf, nbytes)
     handle = exchange_from_rank0(handle, rank, world)
@@ -91,14 +94,16 @@ def _peer_copy_cuda(buf, handle: bytes, nbytes: int) -> float:
     import torch
     from . import _lib
     L = _lib.lib()
-    h = (ctypes.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(handle)
+    h = (ctypes.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(handle[:IPC_HANDLE_BYTES])
+    offset = int.from_bytes(handle[IPC_HANDLE_BYTES:IPC_HANDLE_BYTES + 8], "little")
     peer = ctypes.c_void_p()
     _lib.check(L.cudair_ipc_open(h, ctypes.byref(peer)))
     try:
         s = torch.cuda.current_stream()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        _lib.check(L.cudair_peer_copy(ctypes.c_void_p(buf.data_ptr()), peer, nbytes,
+        _lib.check(L.cudair_peer_copy(ctypes.c_void_p(buf.data_ptr()),
+                                      ctypes.c_void_p(peer.value + offset), nbytes,
                                       ctypes.c_void_p(s.cuda_stream)))
         e1.record()
         torch.cuda.synchronize()

@@ -158,8 +158,9 @@ int cudair_gemm_f16f32(const void *a, const void *b, float *c,
  * Selects the GEMM kernel variant for subsequent calls in this process:
  * 0 = automatic (few-row kernel when M <= 64, CTA pairs with 256 x 256 tiles
  * when M > 128, single CTAs with 128 x 256 tiles in between), 1 = single CTA,
- * 2 = CTA pair, 3 = few-row kernel (M <= 64 only).  All variants compute the
- * same result within fp32 rounding; the choice only affects speed.
+ * 2 = CTA pair, 3 = few-row kernel (M <= 64 only), 4 = CTA pair with
+ * 256 x 512 tiles.  All variants compute the same result within fp32
+ * rounding; the choice only affects speed.
  *
  * The few-row kernel (B as the MMA's 128-row side, K split evenly over all
  * SMs) keeps its partial sums in a 16 MB per-device workspace that the
@@ -222,9 +223,13 @@ int cudair_wait_timeout_selftest(uint64_t limit_ns, void *stream);
 
 #define CUDAIR_IPC_HANDLE_BYTES 64
 
-/* Exports a device allocation for other processes (cudaIpcGetMemHandle). */
-int cudair_ipc_export(const void *dev_ptr, void *handle_out);
-/* Maps another process's allocation into this one (cudaIpcOpenMemHandle). */
+/* Exports the device allocation holding dev_ptr for other processes
+ * (cudaIpcGetMemHandle) and stores dev_ptr's byte offset inside that
+ * allocation in *offset_out: the importer maps the allocation's base, so the
+ * data starts at the mapped pointer + offset. */
+int cudair_ipc_export(const void *dev_ptr, void *handle_out, uint64_t *offset_out);
+/* Maps another process's allocation into this one (cudaIpcOpenMemHandle);
+ * *dev_ptr_out is the allocation's base. */
 int cudair_ipc_open(const void *handle, void **dev_ptr_out);
 /* Unmaps it (cudaIpcCloseMemHandle). */
 int cudair_ipc_close(void *dev_ptr);

@@ -33,11 +33,11 @@ def no_wait_timeouts(dev, cudair):
     assert kernels.wait_status(clear=True) == 0
 
 
-@pytest.fixture(params=[1, 2, 3], ids=["single", "pair", "fewrows"])
+@pytest.fixture(params=[1, 2, 3, 4], ids=["single", "pair", "fewrows", "pairwide"])
 def variant(request, dev, cudair):
     """Runs a test on each GEMM kernel in turn: single CTA (128x256 tiles),
-    CTA pair (256x256) and the few-row kernel (M <= 64), then restores the
-    automatic choice."""
+    CTA pair (256x256), the few-row kernel (M <= 64) and the wide CTA pair
+    (256x512), then restores the automatic choice."""
     from cudair import kernels
     kernels.set_gemm_variant(request.param)
     yield request.param
