@@ -17,8 +17,9 @@
 //     and the last to arrive adds C and the partials in CTA order (so the sum
 //     order, and the result, do not depend on timing), stores C and resets
 //     the counter to zero for the next launch.
-//   * an 8-stage TMA ring of 16 KB B tiles (two 64 x 64 boxes) plus
-//     mpad x 64 A tiles keeps about 180 KB of B in flight per SM.
+//   * a TMA ring of 16 KB B tiles (two 64 x 64 boxes) plus mpad x 64 A tiles,
+//     as many stages as fit (12 at M <= 16), keeps up to 216 KB of B in
+//     flight per SM.
 //
 // Roles as in gemm_sm100.cu (192 threads): warp 0 TMA producer, warp 1 TMEM
 // owner and MMA issuer, warps 2-5 epilogue and fix-up.  All waits are
@@ -37,15 +38,26 @@ namespace skinny {
 
 constexpr int BN_T = 128;  // n per tile (the MMA's M)
 constexpr int BK = 64;
-constexpr int STAGES = 8;
+constexpr int MAX_STAGES = 12;
 constexpr int THREADS = 192;
 constexpr int MAX_M = 64;
 constexpr uint32_t B_BOX_BYTES = 64 * BK * 2;        // 64 n x 64 k
 constexpr uint32_t B_STAGE_BYTES = 2 * B_BOX_BYTES;  // 16 KB
-constexpr uint32_t A_STAGE_MAX = MAX_M * BK * 2;     // 8 KB at mpad = 64
 constexpr uint32_t BAR_BYTES = 256;
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (B_STAGE_BYTES + A_STAGE_MAX) + BAR_BYTES;
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+constexpr size_t SMEM_BYTES = 227 * 1024;  // the launch's dynamic shared memory limit
+
+// The ring holds as many stages of (B tile + this M's A tile) as fit: with
+// M <= 16 that is 12 stages (216 KB of B in flight per SM), with M = 64 nine.
+__host__ __device__ constexpr int stages_for(int mpad) {
+    return static_cast<int>((SMEM_BYTES - 1024 - BAR_BYTES) / (B_STAGE_BYTES + mpad * BK * 2)) < MAX_STAGES
+               ? static_cast<int>((SMEM_BYTES - 1024 - BAR_BYTES) / (B_STAGE_BYTES + mpad * BK * 2))
+               : MAX_STAGES;
+}
+__host__ __device__ constexpr size_t smem_for(int mpad) {
+    return 1024 + static_cast<size_t>(stages_for(mpad)) * (B_STAGE_BYTES + mpad * BK * 2) + BAR_BYTES;
+}
+static_assert(smem_for(16) <= SMEM_BYTES && smem_for(64) <= SMEM_BYTES, "shared memory budget");
+static_assert(2 * MAX_STAGES * 8 + 5 * 8 + 12 <= BAR_BYTES, "barrier area");
 
 // Workspace layout: tile counters first, then two partial slots per CTA.
 constexpr size_t COUNTER_BYTES = 256 * 1024;  // 65536 n-tiles
@@ -68,9 +80,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
 
     const uint32_t a_stage_bytes = static_cast<uint32_t>(mpad) * BK * 2;  // multiple of 1024
+    const int STAGES = stages_for(mpad);
     uint8_t *sB = smem;
     uint8_t *sA = smem + STAGES * B_STAGE_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sA + STAGES * A_STAGE_MAX);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sA + STAGES * a_stage_bytes);
     uint64_t *full = bars;
     uint64_t *empty = bars + STAGES;
     uint64_t *acc_full = bars + 2 * STAGES;
@@ -132,7 +145,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int j = 0; j < nb; ++j)
                     tma_load_2d(sB + stage * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB, &full[stage],
                                 n0 + 64 * j, k0, policy_b);
-                tma_load_2d(sA + stage * A_STAGE_MAX, &tmA, &full[stage], k0, 0, policy_a);
+                tma_load_2d(sA + stage * a_stage_bytes, &tmA, &full[stage], k0, 0, policy_a);
                 ++issued;
                 if (++stage == STAGES) {
                     stage = 0;
@@ -173,7 +186,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     tc_fence_after_sync();
                     const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
-                    const uint32_t a_base = smem_u32(sA + stage * A_STAGE_MAX);
+                    const uint32_t a_base = smem_u32(sA + stage * a_stage_bytes);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         // B^T: MN-major, n-blocks 8 KB apart, k groups 1 KB apart.
@@ -393,7 +406,7 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
     const int grid = static_cast<int>(T < sm_count ? T : sm_count);
     unsigned int *counters = static_cast<unsigned int *>(ws->ptr);
     float *partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws->ptr) + skinny::COUNTER_BYTES);
-    skinny::gemm_skinny_kernel<<<grid, skinny::THREADS, skinny::SMEM_BYTES, stream>>>(
+    skinny::gemm_skinny_kernel<<<grid, skinny::THREADS, skinny::smem_for(mpad), stream>>>(
         tmB, tmA, c, M, N, K, static_cast<long long>(ldc), mpad, counters, partials, status);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch");
@@ -549,7 +562,7 @@ CUDAIR_API int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaMemsetAsync(counters, 0, static_cast<size_t>(n_tiles) * sizeof(unsigned int), s);
     if (e != cudaSuccess) return cuda_error(e, "cudaMemsetAsync(no-alloc tile counters)");
-    skinny::gemm_skinny_kernel<<<static_cast<unsigned>(grid), skinny::THREADS, skinny::SMEM_BYTES, s>>>(
+    skinny::gemm_skinny_kernel<<<static_cast<unsigned>(grid), skinny::THREADS, skinny::smem_for(mpad), s>>>(
         tmB, tmA, c, Mi, Ni, Ki, static_cast<long long>(ldc), mpad, counters, partials, status);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch (no-alloc)");
