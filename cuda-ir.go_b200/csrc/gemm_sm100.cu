@@ -27,12 +27,13 @@
 //              announces a finished accumulator on `acc_full` (multicast to
 //              both CTAs of a pair).
 //   warps 2-5  epilogue: warp w owns TMEM lanes 32 (w mod 4) .. +31 (one row
-//              per thread), reads 32 columns at a time with tcgen05.ld, adds C
-//              (its 16-byte loads issued one chunk ahead, the first before
-//              the accumulator is ready) and stores the sum; the accumulator
-//              is handed back on `acc_empty` (for a pair, the even CTA's,
-//              counting the eight epilogue warps of both CTAs), so tile i's
-//              epilogue overlaps tile i+1's mainloop.
+//              per thread), reads 32 columns at a time with tcgen05.ld,
+//              stages them as a 32 x 32 box in shared memory and hands the
+//              box to a TMA reduce-add, so L2 adds it into C (C is never
+//              loaded into the SM); the accumulator is handed back on
+//              `acc_empty` (for a pair, the even CTA's, counting the eight
+//              epilogue warps of both CTAs) as soon as it is read, so tile
+//              i's epilogue overlaps tile i+1's mainloop.
 // Tiles are visited in groups of row-blocks so that the CTAs resident at one
 // time share A row-panels and B column-panels in L2.
 //
@@ -62,13 +63,16 @@ constexpr uint32_t A_BOX_BYTES = 128 * BK * 2;  // 16 KB: 128 rows x 64 k
 constexpr uint32_t B_BOX_BYTES = 64 * BK * 2;   // 8 KB: 64 n x 64 k
 constexpr uint32_t TMEM_COLS = 2 * BN;           // two accumulators
 constexpr uint32_t BAR_BYTES = 256;
+// Epilogue staging: two 32 x 32 fp32 boxes per epilogue warp.
+constexpr uint32_t EPI_BOX_BYTES = 32 * 32 * 4;
+constexpr uint32_t EPI_BYTES = 4 * 2 * EPI_BOX_BYTES;  // 32 KB
 
 // single-CTA variant
 constexpr int S_BM = 128;
 constexpr int S_STAGES = 4;
 constexpr int S_GROUP_M = 16;
 constexpr uint32_t S_STAGE_B = BN / 64 * B_BOX_BYTES;  // 32 KB
-constexpr size_t S_SMEM = 1024 + S_STAGES * (A_BOX_BYTES + S_STAGE_B) + BAR_BYTES;
+constexpr size_t S_SMEM = 1024 + S_STAGES * (A_BOX_BYTES + S_STAGE_B) + EPI_BYTES + BAR_BYTES;
 
 // CTA-pair variants: NB 256-column MMA blocks per tile (NB = 1: 256 x 256
 // tiles, two accumulators; NB = 2: 256 x 512 tiles, one accumulator filling
@@ -84,10 +88,10 @@ struct PairCfg {
     static constexpr int TILE_N = 256 * NB;
     static constexpr uint32_t STAGE_B = NB * 2 * B_BOX_BYTES;  // this CTA's 128 x NB columns
     static constexpr uint32_t STAGE = A_BOX_BYTES + STAGE_B;
-    static constexpr int STAGES_FIT = static_cast<int>((227 * 1024 - 1024 - BAR_BYTES) / STAGE);
+    static constexpr int STAGES_FIT = static_cast<int>((227 * 1024 - 1024 - EPI_BYTES - BAR_BYTES) / STAGE);
     static constexpr int STAGES = STAGES_FIT < 7 ? STAGES_FIT : 7;
     static constexpr int ACCS = 2 / NB;  // accumulator buffers in 512 TMEM columns
-    static constexpr size_t SMEM = 1024 + STAGES * STAGE + BAR_BYTES;
+    static constexpr size_t SMEM = 1024 + STAGES * STAGE + EPI_BYTES + BAR_BYTES;
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -111,66 +115,51 @@ __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity, unsig
     mbar_wait(bar, parity, &never, status, kSiteDrain);
 }
 
-// C is read once and written once per launch: its accesses skip L1 and are
-// marked first to leave L2, so the stream of C does not push out the A and B
-// panels that other tiles re-read.
+// C is read once and written once per launch, inside L2 by the reduce-add
+// (or by the scalar path's loads and stores): marked first to leave L2, so the
+// stream of C does not push out the A and B panels that other tiles re-read.
 __device__ __forceinline__ uint64_t c_policy() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
 
-__device__ __forceinline__ float4 ld_c(const float *p, uint64_t pol) {
-    float4 v;
-    asm volatile("ld.global.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(p), "l"(pol));
-    return v;
-}
-
-__device__ __forceinline__ void st_c(float *p, float4 v, uint64_t pol) {
-    asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p),
-                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "l"(pol)
-                 : "memory");
-}
-
-// 32 columns of C for this thread's row, as eight 16-byte loads.
-__device__ __forceinline__ void load_c_chunk(float4 (&v)[8], const float *crow, int col, int N,
-                                             bool row_ok, uint64_t pol) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-        v[j] = (row_ok && col + 4 * j < N) ? ld_c(crow + col + 4 * j, pol)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-}
-
 // Adds this warp's 32 accumulator rows (TMEM lanes from t_row, 256 columns)
-// to C and stores the sums.  c_next holds chunk 0 of C, loaded by the caller.
-__device__ __forceinline__ void epilogue_rows_vec4(uint32_t t_row, float *crow, int row, int n0,
-                                                   int M, int N, float4 (&c_next)[8], uint64_t pol) {
-    const bool row_ok = row < M;
-#pragma unroll
+// into C with TMA reduce-add.  Each 32-column chunk goes TMEM -> registers ->
+// a 32 x 32 staging box in shared memory (the 128-byte swizzled layout of
+// tmC, so the row-per-thread stores are free of bank conflicts) -> one
+// cp.reduce.async.bulk.tensor, and L2 adds the box into C: C never enters the
+// SM, and each element of C gets exactly one add, C + (A.B), rounded once.
+// Rows and columns outside C are clipped by the tensor map.  The warp's two
+// boxes alternate (`buf` carries over between calls); lane 0 issues and
+// tracks the bulk groups, and a box is rewritten only after the reduce that
+// last read it has finished reading.
+__device__ __forceinline__ void epilogue_rows_reduce(uint32_t t_row, const CUtensorMap *tmC,
+                                                     uint32_t boxes, int row0, int n0, int N,
+                                                     uint64_t pol, uint32_t &buf) {
+    const uint32_t lane = lane_id();
+#pragma unroll 1
     for (int ch = 0; ch < BN / 32; ++ch) {
-        float4 c_cur[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) c_cur[j] = c_next[j];
-        if (ch + 1 < BN / 32) load_c_chunk(c_next, crow, n0 + (ch + 1) * 32, N, row_ok, pol);
+        const int col = n0 + ch * 32;
+        if (col >= N) break;  // the rest of the block lies beyond C
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + ch * 32, r);
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
         tmem_ld_wait();
-        const int col = n0 + ch * 32;
-        if (row_ok) {
+        const uint32_t box = boxes + buf * EPI_BOX_BYTES;
+        const uint32_t row_addr = box + lane * 128u;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                if (col + 4 * j < N) {
-                    float4 v = c_cur[j];
-                    v.x += __uint_as_float(r[4 * j + 0]);
-                    v.y += __uint_as_float(r[4 * j + 1]);
-                    v.z += __uint_as_float(r[4 * j + 2]);
-                    v.w += __uint_as_float(r[4 * j + 3]);
-                    st_c(crow + col + 4 * j, v, pol);
-                }
-            }
+        for (int j = 0; j < 8; ++j)
+            st_shared_v4(row_addr + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4), r[4 * j],
+                         r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_reduce_add_2d(tmC, box, col, row0, pol);
+            bulk_commit_group();
         }
+        buf ^= 1u;
     }
 }
 
@@ -196,15 +185,17 @@ __device__ __forceinline__ void epilogue_rows_scalar(uint32_t t_row, float *crow
 // =============================================================================
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16f32_kernel(const __grid_constant__ CUtensorMap tmA,
-                       const __grid_constant__ CUtensorMap tmB, float *__restrict__ C, int M,
-                       int N, int K, long long ldc, int vec4) {
+                       const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmC, float *__restrict__ C, int M,
+                       int N, int K, long long ldc, int reduce) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // 1024-aligned tiles
 
     uint8_t *sA = smem;
     uint8_t *sB = smem + S_STAGES * A_BOX_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sB + S_STAGES * S_STAGE_B);
+    uint8_t *sEpi = sB + S_STAGES * S_STAGE_B;  // 1024-aligned staging boxes
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + EPI_BYTES);
     uint64_t *full = bars;
     uint64_t *empty = bars + S_STAGES;
     uint64_t *acc_full = bars + 2 * S_STAGES;
@@ -234,6 +225,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_mbar_init();
         tma_prefetch_map(&tmA);
         tma_prefetch_map(&tmB);
+        if (reduce) tma_prefetch_map(&tmC);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, TMEM_COLS);
@@ -340,29 +332,32 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---------------- epilogue (warps 2..5) ----------------
         const uint32_t q = warp & 3u;  // the TMEM lane quarter this warp may read
         const uint64_t cpol = c_policy();
-        uint32_t acc = 0, acc_phase = 0;
+        const uint32_t boxes = smem_u32(sEpi) + q * 2 * EPI_BOX_BYTES;
+        uint32_t acc = 0, acc_phase = 0, buf = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int m_blk, n_blk;
             tile_coords(t, num_m, num_n, S_GROUP_M, m_blk, n_blk);
             const int m0 = m_blk * S_BM, n0 = n_blk * BN;
-            const int row = m0 + static_cast<int>(q * 32 + lane);
-            float *crow = C + static_cast<long long>(row) * ldc;
-            float4 c_next[8];
-            if (vec4) load_c_chunk(c_next, crow, n0, N, row < M, cpol);
+            const int row0 = m0 + static_cast<int>(q * 32);
             if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull))
                 break;
             tc_fence_after_sync();
             const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
-            if (vec4)
-                epilogue_rows_vec4(t_row, crow, row, n0, M, N, c_next, cpol);
-            else
-                epilogue_rows_scalar(t_row, crow, row, n0, M, N);
+            if (reduce) {
+                if (row0 < M) epilogue_rows_reduce(t_row, &tmC, boxes, row0, n0, N, cpol, buf);
+            } else {
+                const int row = row0 + static_cast<int>(lane);
+                epilogue_rows_scalar(t_row, C + static_cast<long long>(row) * ldc, row, n0, M, N);
+            }
             tc_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
             acc ^= 1u;
             if (acc == 0) acc_phase ^= 1u;
         }
+        // The reduces still in flight read this CTA's shared memory: they
+        // finish before the CTA exits.
+        if (lane == 0) bulk_wait_group<0>();
         __syncwarp();
     }
 
@@ -380,8 +375,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 template <int NB>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                            const __grid_constant__ CUtensorMap tmB, float *__restrict__ C, int M,
-                            int N, int K, long long ldc, int vec4) {
+                            const __grid_constant__ CUtensorMap tmB,
+                            const __grid_constant__ CUtensorMap tmC, float *__restrict__ C, int M,
+                            int N, int K, long long ldc, int reduce) {
     using Cfg = PairCfg<NB>;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -390,7 +386,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_BOX_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * Cfg::STAGE_B);
+    uint8_t *sEpi = sB + STAGES * Cfg::STAGE_B;  // 1024-aligned staging boxes
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + EPI_BYTES);
     uint64_t *full = bars;                     // used in the even CTA only
     uint64_t *empty = bars + STAGES;           // both CTAs
     uint64_t *acc_full = bars + 2 * STAGES;    // both CTAs
@@ -425,6 +422,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_mbar_init();
         tma_prefetch_map(&tmA);
         tma_prefetch_map(&tmB);
+        if (reduce) tma_prefetch_map(&tmC);
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -552,15 +550,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---------------- epilogue (warps 2..5, both CTAs) ----------------
         const uint32_t q = warp & 3u;
         const uint64_t cpol = c_policy();
-        uint32_t acc = 0, acc_phase = 0;
+        const uint32_t boxes = smem_u32(sEpi) + q * 2 * EPI_BOX_BYTES;
+        uint32_t acc = 0, acc_phase = 0, buf = 0;
         for (int t = cluster; t < num_tiles; t += num_clusters) {
             int m_blk, n_blk;
             tile_coords(t, num_m, num_n, P_GROUP_M, m_blk, n_blk);
             const int m0 = m_blk * P_BM + 128 * static_cast<int>(rank), n0 = n_blk * Cfg::TILE_N;
-            const int row = m0 + static_cast<int>(q * 32 + lane);
-            float *crow = C + static_cast<long long>(row) * ldc;
-            float4 c_next[8];
-            if (vec4) load_c_chunk(c_next, crow, n0, N, row < M, cpol);
+            const int row0 = m0 + static_cast<int>(q * 32);
             if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, status,
                            kSiteEpilogueAccFull)) {
                 give_up();
@@ -570,11 +566,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * 256;
 #pragma unroll 1
             for (int h = 0; h < NB; ++h) {
-                if (vec4) {
-                    if (h > 0) load_c_chunk(c_next, crow, n0 + 256 * h, N, row < M, cpol);
-                    epilogue_rows_vec4(t_row + 256 * h, crow, row, n0 + 256 * h, M, N, c_next, cpol);
+                if (reduce) {
+                    if (row0 < M)
+                        epilogue_rows_reduce(t_row + 256 * h, &tmC, boxes, row0, n0 + 256 * h, N,
+                                             cpol, buf);
                 } else {
-                    epilogue_rows_scalar(t_row + 256 * h, crow, row, n0 + 256 * h, M, N);
+                    const int row = row0 + static_cast<int>(lane);
+                    epilogue_rows_scalar(t_row + 256 * h, C + static_cast<long long>(row) * ldc, row,
+                                         n0 + 256 * h, M, N);
                 }
             }
             tc_fence_before_sync();
@@ -583,6 +582,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (Cfg::ACCS == 2) acc ^= 1u;
             if (acc == 0) acc_phase ^= 1u;
         }
+        if (lane == 0) bulk_wait_group<0>();  // reduces in flight read this CTA's boxes
         __syncwarp();
     }
 
@@ -758,7 +758,20 @@ int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_
         if (rc != CUDAIR_OK) return rc;
     }
 
-    const int vec4 = ((reinterpret_cast<uintptr_t>(c) & 15u) == 0 && ldc % 4 == 0 && N % 4 == 0) ? 1 : 0;
+    // C takes the TMA reduce-add epilogue when a tensor map can describe it
+    // (16-byte aligned base and row pitch); otherwise scalar loads and stores.
+    const int reduce = ((reinterpret_cast<uintptr_t>(c) & 15u) == 0 && ldc % 4 == 0) ? 1 : 0;
+    alignas(64) CUtensorMap tmC = {};
+    if (reduce) {
+        const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(ldc) * 4};
+        const uint32_t box[2] = {32, 32};
+        rc = encode_tiled_internal(&tmC, CUDAIR_TENSOR_MAP_FLOAT32, 2,
+                                   reinterpret_cast<uint64_t>(c), dims, strides, box, nullptr,
+                                   CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B,
+                                   CUDAIR_L2_PROMOTION_NONE, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
     const int Mi = static_cast<int>(M), Ni = static_cast<int>(N), Ki = static_cast<int>(K);
     const long long ldcl = static_cast<long long>(ldc);
     cudaError_t e;
@@ -779,17 +792,19 @@ int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_
         cfg.numAttrs = 1;
         if (pair_nb == 2) {
             cfg.dynamicSmemBytes = gemm::PairCfg<2>::SMEM;
-            e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<2>, tmA, tmB, c, Mi, Ni, Ki, ldcl, vec4);
+            e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<2>, tmA, tmB, tmC, c, Mi, Ni, Ki, ldcl,
+                                   reduce);
         } else {
             cfg.dynamicSmemBytes = gemm::PairCfg<1>::SMEM;
-            e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<1>, tmA, tmB, c, Mi, Ni, Ki, ldcl, vec4);
+            e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<1>, tmA, tmB, tmC, c, Mi, Ni, Ki, ldcl,
+                                   reduce);
         }
         if (e != cudaSuccess) return cuda_error(e, "gemm_f16f32_pair_kernel launch");
     } else {
         const int64_t tiles = ((M + gemm::S_BM - 1) / gemm::S_BM) * ((N + gemm::BN - 1) / gemm::BN);
         const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
-        gemm::gemm_f16f32_kernel<<<grid, gemm::THREADS, gemm::S_SMEM, stream>>>(tmA, tmB, c, Mi, Ni,
-                                                                                 Ki, ldcl, vec4);
+        gemm::gemm_f16f32_kernel<<<grid, gemm::THREADS, gemm::S_SMEM, stream>>>(
+            tmA, tmB, tmC, c, Mi, Ni, Ki, ldcl, reduce);
         e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_error(e, "gemm_f16f32_kernel launch");
     }

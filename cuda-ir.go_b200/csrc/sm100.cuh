@@ -116,6 +116,44 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
+// 2D tile reduce-add shared -> global: L2 adds the box element-wise into the
+// tensor (fp32 add, round to nearest); elements outside the tensor are
+// skipped.  x (innermost) * element size must be a multiple of 16 bytes and
+// neither coordinate may be negative.  Tracked by the bulk-group mechanism.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, uint32_t smem_src,
+                                                  int32_t x, int32_t y, uint64_t cache_hint) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group.L2::cache_hint"
+        " [%0, {%2, %3}], [%1], %4;" ::"l"(reinterpret_cast<uint64_t>(map)),
+        "r"(smem_src), "r"(x), "r"(y), "l"(cache_hint)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N of this thread's committed bulk groups are still
+// reading their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N of this thread's committed bulk groups are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) reads of them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
 // L2 eviction-priority policies for the cache hints above.
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     uint64_t p;

@@ -274,3 +274,28 @@ def test_fewrows_deterministic_and_within_tolerance(dev, cudair, oracle, M, N, K
     tol_rel, tol_max = oracle.gemm_tolerance(K, np.abs(af).max(), np.abs(bf).max())
     rel, mx, bad = oracle.error_norms(outs[0], want)
     assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
+
+
+@pytest.mark.parametrize("c_offset,ldc_pad", [(0, 2), (1, 0), (3, 5)], ids=["odd-n", "c+4B", "c+12B-odd-ldc"])
+def test_gemm_c_layouts(dev, cudair, variant, c_offset, ldc_pad):
+    # C views the reduce-add epilogue must clip (N not a multiple of 4) or
+    # cannot describe (a base or row pitch not on 16 bytes: scalar path).
+    # Elements of C outside the view keep their value.
+    import torch
+    from cudair import kernels
+    M = 40 if variant == 3 else 300
+    N, K = 101, 136
+    af, bf, c, want = kat(M, N, K)
+    A = _dev(af, dev, torch.float16)
+    B = torch.zeros(K, 104, dtype=torch.float16, device=dev)
+    B[:, :N] = _dev(bf, dev, torch.float16)
+    ldc = N + ldc_pad
+    flat = torch.full((c_offset + M * ldc + 8,), -7.0, dtype=torch.float32, device=dev)
+    C = flat[c_offset:c_offset + M * ldc].view(M, ldc)[:, :N]
+    C.copy_(_dev(c, dev, torch.float32))
+    kernels.gemm(A, B[:, :N], C)
+    got = flat.cpu().numpy()
+    body = got[c_offset:c_offset + M * ldc].reshape(M, ldc)
+    assert np.array_equal(body[:, :N], want)
+    assert np.all(body[:, N:] == -7.0)
+    assert np.all(got[:c_offset] == -7.0) and np.all(got[c_offset + M * ldc:] == -7.0)
