@@ -3,16 +3,18 @@
 // the operation of MatMul16 (examples/hopper/hopper.go:194-226) for any
 // M, N, K, as persistent, warp-specialised tcgen05 kernels for sm_100a.
 //
-// Two variants share the roles, the tile order and the epilogue:
+// Three variants share the roles, the tile order and the epilogue:
 //
-//   pair (default for M > 128): clusters of two CTAs on two SMs compute
-//     256 x 256 tiles with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16).
-//     Each CTA loads its own 128 rows of A and its own 128 columns of B (no
+//   pair (M > 128): clusters of two CTAs on two SMs compute 256 x 256 tiles
+//     with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16).  Each CTA
+//     loads its own 128 rows of A and its own 128 columns of B (no
 //     multicast), so a CTA moves 32 KB per 64-wide k-block instead of 48 KB;
-//     seven 32 KB stages fit in shared memory.  The even CTA issues the MMAs.
-//   pair, wide: the same with 256 x 512 tiles (two N = 256 MMAs per k-step
-//     into one accumulator that fills TMEM; each CTA loads 48 KB per k-block
-//     for twice the FLOPs, a four-stage ring).
+//     six 32 KB stages fit beside the epilogue's staging boxes.  The even CTA
+//     issues the MMAs.
+//   pair, wide (M > 128, large K): the same with 256 x 512 tiles (two N = 256
+//     MMAs per k-step into one accumulator that fills TMEM; each CTA loads
+//     48 KB per k-block for twice the FLOPs, a four-stage ring).  The
+//     launcher picks between the two pair tiles with a makespan estimate.
 //   single (M <= 128): one CTA per SM computes 128 x 256 tiles with
 //     tcgen05.mma.cta_group::1 from a four-stage ring of 48 KB stages.
 //
@@ -79,10 +81,6 @@ constexpr size_t S_SMEM = 1024 + S_STAGES * (A_BOX_BYTES + S_STAGE_B) + EPI_BYTE
 // TMEM, a quarter fewer operand bytes per FLOP).
 constexpr int P_BM = 256;  // rows per pair tile, 128 per CTA
 constexpr int P_GROUP_M = 8;
-// The CTA-pair tile the automatic choice uses (1: 256 x 256, 2: 256 x 512).
-#ifndef CUDAIR_AUTO_PAIR_NB
-#define CUDAIR_AUTO_PAIR_NB 1
-#endif
 template <int NB>
 struct PairCfg {
     static constexpr int TILE_N = 256 * NB;
@@ -701,6 +699,24 @@ int sm_count_current_device(int *count) {
     return CUDAIR_OK;
 }
 
+namespace gemm {
+// The CTA-pair tile for a shape: 256 x 512 tiles (2) move a quarter fewer
+// operand bytes per FLOP, but their accumulator fills TMEM, so each tile's
+// epilogue is not overlapped, and they come in half as many tiles.  The choice
+// compares the estimated makespan, persistent waves x time per tile, with
+// per-tile times fitted on B200 (microseconds, K in elements):
+//   256 x 256: 0.00703 K + 3.4     256 x 512: 0.0124 K + 11.6
+// (8192^3: 14 waves x 61.0 us against 7 x 113.2 us).
+int auto_pair_nb(int64_t M, int64_t N, int64_t K, int pairs) {
+    const int64_t mt = (M + P_BM - 1) / P_BM;
+    const int64_t w1 = (mt * ((N + 255) / 256) + pairs - 1) / pairs;
+    const int64_t w2 = (mt * ((N + 511) / 512) + pairs - 1) / pairs;
+    const double t1 = static_cast<double>(w1) * (0.00703 * static_cast<double>(K) + 3.4);
+    const double t2 = static_cast<double>(w2) * (0.0124 * static_cast<double>(K) + 11.6);
+    return t2 < t1 ? 2 : 1;
+}
+}  // namespace gemm
+
 int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K,
                        int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t stream) {
     if (M < 0 || N < 0 || K < 0)
@@ -734,7 +750,10 @@ int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_
                                   stream);
     // 0 auto, 1 single CTA, 2 CTA pair (256 x 256), 4 CTA pair (256 x 512).
     const bool pair_auto = variant == 0 && M > 128 && dev->max_pairs > 0;
-    const int pair_nb = (variant == 4) ? 2 : ((variant == 2 || pair_auto) ? CUDAIR_AUTO_PAIR_NB : 0);
+    const int pair_nb = (variant == 4) ? 2
+                        : (variant == 2) ? 1
+                        : pair_auto ? gemm::auto_pair_nb(M, N, K, dev->max_pairs)
+                                    : 0;
     const bool pair = pair_nb > 0;
     alignas(64) CUtensorMap tmA, tmB;
     {
