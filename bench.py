@@ -323,27 +323,25 @@ def workload_config(n_gpus):
 
 
 def run_e2e(args, world, dev, a, b, c, flops, kernels):
-    """The GEMM step through the C ABI from pinned host buffers: H2D of A, B
-    and C, the launch, D2H of C, all inside the timed region."""
+    """The GEMM step from pinned host buffers through the C ABI's host entry
+    (cudair_gemm_f16f32_host): every step copies A, B and C in, multiplies
+    and copies C back to the host, all inside the timed region, with the
+    copies of one block of rows overlapping the GEMM of the previous one."""
     import torch
     a_h = a.cpu().pin_memory()
     b_h = b.cpu().pin_memory()
     c_h = c.cpu().pin_memory()
-    c_out = torch.empty_like(c_h).pin_memory()
     a_d, b_d, c_d = torch.empty_like(a), torch.empty_like(b), torch.empty_like(c)
 
     def e2e_step():
-        a_d.copy_(a_h, non_blocking=True)
-        b_d.copy_(b_h, non_blocking=True)
-        c_d.copy_(c_h, non_blocking=True)
-        kernels.gemm(a_d, b_d, c_d)
-        c_out.copy_(c_d, non_blocking=True)
+        kernels.gemm_host(a_h, b_h, c_h, a_d, b_d, c_d)
 
     steps = max(3, min(args.steps, 20))
     ms = time_steps(e2e_step, steps, 3, world, dev)
     return {"value": flops * world / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
             "h2d_bytes_per_step": a_h.numel() * 2 + b_h.numel() * 2 + c_h.numel() * 4,
-            "d2h_bytes_per_step": c_out.numel() * 4, "ms_per_step": ms, "steps": steps}
+            "d2h_bytes_per_step": c_h.numel() * 4, "ms_per_step": ms, "steps": steps,
+            "api": "cudair_gemm_f16f32_host (row blocks of 512: H2D, GEMM and D2H overlapped)"}
 
 
 def run_gather(world, dev, M, N):

@@ -1,0 +1,168 @@
+// host_gemm.cu - C = A.B + C from host buffers, the flow of the reference's
+// MatMul16 test (advanced_test.go:466-483: copy A, B and C to the device,
+// launch, copy C back) as one call whose copies overlap the GEMM.
+//
+// The rows of A and C are cut into blocks.  Three streams carry the work:
+//   in       H2D of B, then of each block of A and C, in order;
+//   caller   the GEMM of block i once B and block i have landed;
+//   out      D2H of block i of C once its GEMM is done.
+// So block i+1 crosses the host link while block i is multiplied and block
+// i-1 travels back: the step costs about its H2D bytes at link speed instead
+// of H2D + GEMM + D2H in series.  The caller's stream waits for the last copy
+// out, so synchronising that stream covers the whole call.
+//
+// The caller owns every buffer; the library keeps two streams and a set of
+// events per device, created on first use.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "cudair_internal.h"
+
+namespace cudair {
+namespace {
+
+constexpr int kMaxBlocks = 64;
+
+struct HostPipe {
+    cudaStream_t in = nullptr, out = nullptr;
+    cudaEvent_t start = nullptr, b_in = nullptr;
+    cudaEvent_t block_in[kMaxBlocks], block_done[kMaxBlocks], block_out[kMaxBlocks];
+    bool ready = false;
+};
+
+std::mutex g_pipe_mu;
+HostPipe g_pipe[64];
+
+int make_event(cudaEvent_t *e) {
+    cudaError_t r = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
+    return r == cudaSuccess ? CUDAIR_OK : cuda_error(r, "cudaEventCreateWithFlags");
+}
+
+// The pipe of the current device; called with g_pipe_mu held.
+int pipe_for_current_device(HostPipe **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return set_error(CUDAIR_ERR_INVALID, "cudair: device index %d out of range", dev);
+    HostPipe &p = g_pipe[dev];
+    if (!p.ready) {
+        if ((e = cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking)) != cudaSuccess)
+            return cuda_error(e, "cudaStreamCreateWithFlags");
+        if ((e = cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking)) != cudaSuccess)
+            return cuda_error(e, "cudaStreamCreateWithFlags");
+        int rc = make_event(&p.start);
+        if (rc == CUDAIR_OK) rc = make_event(&p.b_in);
+        for (int i = 0; i < kMaxBlocks && rc == CUDAIR_OK; ++i) {
+            rc = make_event(&p.block_in[i]);
+            if (rc == CUDAIR_OK) rc = make_event(&p.block_done[i]);
+            if (rc == CUDAIR_OK) rc = make_event(&p.block_out[i]);
+        }
+        if (rc != CUDAIR_OK) return rc;
+        p.ready = true;
+    }
+    *out = &p;
+    return CUDAIR_OK;
+}
+
+// rows x row_bytes between buffers with pitches dpitch / spitch.
+cudaError_t copy_rows(void *dst, size_t dpitch, const void *src, size_t spitch, size_t row_bytes,
+                      size_t rows, cudaMemcpyKind kind, cudaStream_t s) {
+    if (dpitch == row_bytes && spitch == row_bytes)
+        return cudaMemcpyAsync(dst, src, row_bytes * rows, kind, s);
+    return cudaMemcpy2DAsync(dst, dpitch, src, spitch, row_bytes, rows, kind, s);
+}
+
+}  // namespace
+}  // namespace cudair
+
+using namespace cudair;
+
+CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, float *c_host,
+                                       int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                                       int64_t ldc, void *a_dev, void *b_dev, float *c_dev,
+                                       int64_t rows_per_block, void *stream) {
+    clear_error();
+    if (M < 0 || N < 0 || K < 0)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_host: negative size M=%lld N=%lld K=%lld",
+                         (long long)M, (long long)N, (long long)K);
+    if (M == 0 || N == 0) return CUDAIR_OK;  // C has no elements
+    if (!a_host || !b_host || !c_host || !a_dev || !b_dev || !c_dev)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_host: nil pointer");
+    if (lda < K || ldb < N || ldc < N)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm_host: host leading dimensions lda=%lld ldb=%lld ldc=%lld too small",
+                         (long long)lda, (long long)ldb, (long long)ldc);
+    if (K % 8 || N % 8)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm_host: K=%lld and N=%lld must be multiples of 8 (the device "
+                         "copies are dense, with 16-byte rows)",
+                         (long long)K, (long long)N);
+    if (rows_per_block < 0)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_host: rows_per_block = %lld",
+                         (long long)rows_per_block);
+    // Blocks of whole 256-row pair tiles, at most kMaxBlocks of them; by
+    // default about sixteen, so the copy out of the last block (the part of
+    // the call nothing overlaps) stays short.
+    int64_t rb = rows_per_block;
+    if (rb == 0) rb = (M + 15) / 16;
+    rb = (rb + 255) / 256 * 256;
+    if ((M + rb - 1) / rb > kMaxBlocks) rb = ((M + kMaxBlocks - 1) / kMaxBlocks + 255) / 256 * 256;
+    const int blocks = static_cast<int>((M + rb - 1) / rb);
+
+    int rc = ensure_context();
+    if (rc != CUDAIR_OK) return rc;
+    std::lock_guard<std::mutex> lk(g_pipe_mu);  // the events are shared per device
+    HostPipe *p = nullptr;
+    if ((rc = pipe_for_current_device(&p)) != CUDAIR_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+#define CUDAIR_TRY(call, what)                                 \
+    do {                                                       \
+        if ((e = (call)) != cudaSuccess) return cuda_error(e, what); \
+    } while (0)
+
+    // Nothing is copied in before earlier work on the caller's stream (which
+    // may still read these device buffers) is done.
+    CUDAIR_TRY(cudaEventRecord(p->start, s), "cudaEventRecord");
+    CUDAIR_TRY(cudaStreamWaitEvent(p->in, p->start, 0), "cudaStreamWaitEvent");
+    CUDAIR_TRY(cudaStreamWaitEvent(p->out, p->start, 0), "cudaStreamWaitEvent");
+    const size_t a_row = static_cast<size_t>(K) * 2, b_row = static_cast<size_t>(N) * 2,
+                 c_row = static_cast<size_t>(N) * 4;
+    if (K > 0) {
+        CUDAIR_TRY(copy_rows(b_dev, b_row, b_host, static_cast<size_t>(ldb) * 2, b_row,
+                             static_cast<size_t>(K), cudaMemcpyHostToDevice, p->in),
+                   "H2D of B");
+        CUDAIR_TRY(cudaEventRecord(p->b_in, p->in), "cudaEventRecord");
+        CUDAIR_TRY(cudaStreamWaitEvent(s, p->b_in, 0), "cudaStreamWaitEvent");
+    }
+    for (int i = 0; i < blocks; ++i) {
+        const int64_t r0 = i * rb, rows = (M - r0 < rb) ? M - r0 : rb;
+        uint8_t *a_blk = static_cast<uint8_t *>(a_dev) + static_cast<size_t>(r0) * a_row;
+        float *c_blk = c_dev + static_cast<size_t>(r0) * N;
+        if (K > 0)
+            CUDAIR_TRY(copy_rows(a_blk, a_row,
+                                 static_cast<const uint8_t *>(a_host) + static_cast<size_t>(r0) * lda * 2,
+                                 static_cast<size_t>(lda) * 2, a_row, static_cast<size_t>(rows),
+                                 cudaMemcpyHostToDevice, p->in),
+                       "H2D of a block of A");
+        CUDAIR_TRY(copy_rows(c_blk, c_row, c_host + static_cast<size_t>(r0) * ldc,
+                             static_cast<size_t>(ldc) * 4, c_row, static_cast<size_t>(rows),
+                             cudaMemcpyHostToDevice, p->in),
+                   "H2D of a block of C");
+        CUDAIR_TRY(cudaEventRecord(p->block_in[i], p->in), "cudaEventRecord");
+        CUDAIR_TRY(cudaStreamWaitEvent(s, p->block_in[i], 0), "cudaStreamWaitEvent");
+        rc = gemm_f16f32_launch(a_blk, b_dev, c_blk, rows, N, K, K, N, N, s);
+        if (rc != CUDAIR_OK) return rc;
+        CUDAIR_TRY(cudaEventRecord(p->block_done[i], s), "cudaEventRecord");
+        CUDAIR_TRY(cudaStreamWaitEvent(p->out, p->block_done[i], 0), "cudaStreamWaitEvent");
+        CUDAIR_TRY(copy_rows(c_host + static_cast<size_t>(r0) * ldc, static_cast<size_t>(ldc) * 4,
+                             c_blk, c_row, c_row, static_cast<size_t>(rows), cudaMemcpyDeviceToHost,
+                             p->out),
+                   "D2H of a block of C");
+        CUDAIR_TRY(cudaEventRecord(p->block_out[i], p->out), "cudaEventRecord");
+    }
+    CUDAIR_TRY(cudaStreamWaitEvent(s, p->block_out[blocks - 1], 0), "cudaStreamWaitEvent");
+#undef CUDAIR_TRY
+    return CUDAIR_OK;
+}

@@ -156,10 +156,11 @@ int cudair_gemm_f16f32(const void *a, const void *b, float *c,
 
 /*
  * Selects the GEMM kernel variant for subsequent calls in this process:
- * 0 = automatic (few-row kernel when M <= 64, CTA pairs with 256 x 256 tiles
- * when M > 128, single CTAs with 128 x 256 tiles in between), 1 = single CTA,
- * 2 = CTA pair, 3 = few-row kernel (M <= 64 only), 4 = CTA pair with
- * 256 x 512 tiles.  All variants compute the same result within fp32
+ * 0 = automatic (few-row kernel when M <= 64, single CTAs with 128 x 256
+ * tiles when M <= 128, else CTA pairs with 256 x 256 or 256 x 512 tiles,
+ * whichever a makespan estimate for the shape favours), 1 = single CTA,
+ * 2 = CTA pair with 256 x 256 tiles, 3 = few-row kernel (M <= 64 only),
+ * 4 = CTA pair with 256 x 512 tiles.  All variants compute the same result within fp32
  * rounding; the choice only affects speed.
  *
  * The few-row kernel (B as the MMA's 128-row side, K split evenly over all
@@ -168,6 +169,27 @@ int cudair_gemm_f16f32(const void *a, const void *b, float *c,
  * must not overlap in time (issue them on one stream).
  */
 int cudair_set_gemm_variant(int variant);
+
+/*
+ * C = A.B + C from host buffers: the flow of the reference's MatMul16 test
+ * (advanced_test.go:466-483, which copies A, B and C to the device with
+ * gocudrv CopyFrom, launches MatMul16 and copies C back with CopyTo) as one
+ * call.  a_host (M x K fp16, pitch lda), b_host (K x N fp16, pitch ldb) and
+ * c_host (M x N fp32, pitch ldc) are host memory (page-locked for the copies
+ * to overlap); a_dev, b_dev and c_dev are the caller's device buffers for
+ * dense copies (pitches K, N and N; 16-byte aligned), so K and N must be
+ * multiples of 8.  The rows of A and C are cut into blocks of rows_per_block
+ * (rounded up to 256; 0 = about M / 16), and block i+1 is copied in while
+ * block i is multiplied (cudair_gemm_f16f32, the automatic choice) and block
+ * i-1 is copied out, on two library-owned streams per device.  The call is
+ * asynchronous: `stream` waits for the last copy out, so synchronising it
+ * means C is back in c_host.  Allocates nothing.
+ */
+int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, float *c_host,
+                            int64_t M, int64_t N, int64_t K,
+                            int64_t lda, int64_t ldb, int64_t ldc,
+                            void *a_dev, void *b_dev, float *c_dev,
+                            int64_t rows_per_block, void *stream);
 
 /*
  * The few-row GEMM (1 <= M <= 64, N <= 524288) without any device

@@ -108,6 +108,26 @@ def test_gemm_empty_sizes_are_noops(cudair):
         assert cudair.lib().cudair_gemm_f16f32(None, None, None, M, N, K, 8, 8, 8, None) == 0
 
 
+@pytest.mark.parametrize("size,lds,ptrs,rpb,needle", [
+    ((16, 16, -1), (16, 16, 16), 16, 0, "negative size"),
+    ((16, 16, 16), (8, 16, 16), 16, 0, "host leading dimensions"),
+    ((16, 12, 16), (16, 12, 12), 16, 0, "multiples of 8"),
+    ((16, 16, 16), (16, 16, 16), None, 0, "nil pointer"),
+    ((16, 16, 16), (16, 16, 16), 16, -256, "rows_per_block"),
+])
+def test_gemm_host_validation(cudair, size, lds, ptrs, rpb, needle):
+    # Argument checks come before any CUDA call, so they run without a GPU.
+    M, N, K = size
+    rc = cudair.lib().cudair_gemm_f16f32_host(16, 16, 16, M, N, K, *lds, 16, 16, ptrs, rpb, None)
+    assert rc == 1 and needle in cudair.last_error(), cudair.last_error()
+
+
+def test_gemm_host_empty_c_is_noop(cudair):
+    for M, N in ((0, 8), (8, 0)):
+        assert cudair.lib().cudair_gemm_f16f32_host(None, None, None, M, N, 8, 8, 8, 8,
+                                                    None, None, None, 0, None) == 0
+
+
 def test_vecadd_and_reduce_validation(cudair):
     L = cudair.lib()
     assert L.cudair_vecadd(None, None, None, -1, None) == 1
