@@ -236,67 +236,101 @@ __global__ void __launch_bounds__(THREADS, 1)
             named_bar_sync(1, 128);
             if (!ok || *abort_flag) break;
             tc_fence_after_sync();
+            // This thread's column of the accumulator (row m of C in own[m]).
             const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * static_cast<uint32_t>(mpad);
-            float *part = partials + (static_cast<size_t>(c) * 2 + slot) * BN_T * mpad;
-            for (int j = 0; j < mpad / 16; ++j) {
-                uint32_t r[16];
-                tmem_ld_32x32b_x16(t_row + 16 * j, r);
-                tmem_ld_wait();
+            uint32_t own[MAX_M];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int m = 16 * j + i;
-                    if (whole) {
-                        if (m < M && n < N) {
-                            float *p = C + static_cast<long long>(m) * ldc + n;
-                            *p = *p + __uint_as_float(r[i]);
-                        }
-                    } else {
-                        part[m * BN_T + nl] = __uint_as_float(r[i]);
-                    }
-                }
-            }
+            for (int j = 0; j < MAX_M / 16; ++j)
+                if (16 * j < mpad)
+                    tmem_ld_32x32b_x16(t_row + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(own + 16 * j));
+            tmem_ld_wait();
             tc_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
             acc ^= 1u;
             if (acc == 0) acc_phase ^= 1u;
-            if (whole) continue;
 
-            // Partial tile: count in; the last contributor reduces in CTA order.
-            __threadfence();
-            named_bar_sync(1, 128);
-            const int c_lo = cta_of(tile_lo, T, G), c_hi = cta_of(tile_hi - 1, T, G);
-            if (leader) {
-                const unsigned int prev = atomicAdd(&counters[t], 1u);
-                *last_flag = (prev == static_cast<unsigned int>(c_hi - c_lo)) ? 1 : 0;
-            }
-            named_bar_sync(1, 128);
-            if (*last_flag) {
-                __threadfence();
-                // Sixteen rows at a time: C and then each contributor's
-                // partials are loaded as independent batches (one memory
-                // latency per contributor, not per element) and added in
-                // contributor order.
+            if (whole) {
                 if (n < N) {
-                    for (int m0 = 0; m0 < M; m0 += 16) {
+#pragma unroll
+                    for (int j = 0; j < MAX_M / 16; ++j) {
+                        if (16 * j >= M) break;
                         float v[16];
 #pragma unroll
                         for (int i = 0; i < 16; ++i)
-                            v[i] = (m0 + i < M) ? C[static_cast<long long>(m0 + i) * ldc + n] : 0.f;
-                        for (int cc = c_lo; cc <= c_hi; ++cc) {
-                            const long long s_cc = range_start(cc, T, G);
-                            const int sl = (s_cc / num_kb == t) ? 0 : 1;
-                            const float *pc = partials + (static_cast<size_t>(cc) * 2 + sl) * BN_T * mpad;
-                            float pv[16];
+                            v[i] = (16 * j + i < M) ? C[static_cast<long long>(16 * j + i) * ldc + n] : 0.f;
 #pragma unroll
-                            for (int i = 0; i < 16; ++i)
-                                pv[i] = (m0 + i < M) ? __ldcg(pc + (m0 + i) * BN_T + nl) : 0.f;
+                        for (int i = 0; i < 16; ++i)
+                            if (16 * j + i < M)
+                                C[static_cast<long long>(16 * j + i) * ldc + n] = v[i] + __uint_as_float(own[16 * j + i]);
+                    }
+                }
+                continue;
+            }
+
+            // Partial tile.  Contributors c_lo .. c_hi; the one that finishes
+            // last adds C and every contributor's part in CTA order (so the
+            // result does not depend on timing) and resets the tile counter.
+            // Each other contributor writes its part to the workspace, makes
+            // it visible and counts itself in.  A contributor that finds all
+            // the others counted in already is last without writing its part.
+            const int c_lo = cta_of(tile_lo, T, G), c_hi = cta_of(tile_hi - 1, T, G);
+            const unsigned int others = static_cast<unsigned int>(c_hi - c_lo);
+            if (leader) *last_flag = (ld_acquire_gpu_u32(&counters[t]) == others) ? 1 : 0;
+            named_bar_sync(1, 128);
+            bool last = *last_flag != 0;
+            if (!last) {
+                float *part = partials + (static_cast<size_t>(c) * 2 + slot) * BN_T * mpad;
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) v[i] += pv[i];
+                for (int m = 0; m < MAX_M; ++m)
+                    if (m < mpad) part[m * BN_T + nl] = __uint_as_float(own[m]);
+                __threadfence();
+                named_bar_sync(1, 128);
+                if (leader) {
+                    const unsigned int prev = atomicAdd(&counters[t], 1u);
+                    *last_flag = (prev == others) ? 1 : 0;
+                }
+                named_bar_sync(1, 128);
+                last = *last_flag != 0;
+            }
+            if (last) {
+                __threadfence();
+                // Sixteen rows at a time: C and up to four contributors'
+                // parts are loaded together (one memory latency per four
+                // contributors), then added in contributor order.
+                if (n < N) {
+#pragma unroll
+                    for (int j = 0; j < MAX_M / 16; ++j) {
+                        if (16 * j >= M) break;
+                        float v[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            v[i] = (16 * j + i < M) ? C[static_cast<long long>(16 * j + i) * ldc + n] : 0.f;
+                        for (int cb = c_lo; cb <= c_hi; cb += 4) {
+                            float pv[4][16];
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const int cc = cb + k;
+                                if (cc > c_hi || cc == c) continue;
+                                const long long s_cc = range_start(cc, T, G);
+                                const int sl = (s_cc / num_kb == t) ? 0 : 1;
+                                const float *pc = partials + (static_cast<size_t>(cc) * 2 + sl) * BN_T * mpad;
+#pragma unroll
+                                for (int i = 0; i < 16; ++i)
+                                    pv[k][i] = (16 * j + i < M) ? __ldcg(pc + (16 * j + i) * BN_T + nl) : 0.f;
+                            }
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const int cc = cb + k;
+                                if (cc > c_hi) break;
+#pragma unroll
+                                for (int i = 0; i < 16; ++i)
+                                    v[i] += (cc == c) ? __uint_as_float(own[16 * j + i]) : pv[k][i];
+                            }
                         }
 #pragma unroll
                         for (int i = 0; i < 16; ++i)
-                            if (m0 + i < M) C[static_cast<long long>(m0 + i) * ldc + n] = v[i];
+                            if (16 * j + i < M) C[static_cast<long long>(16 * j + i) * ldc + n] = v[i];
                     }
                 }
                 if (leader) counters[t] = 0u;

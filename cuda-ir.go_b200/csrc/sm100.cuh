@@ -154,6 +154,15 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                  : "memory");
 }
 
+// Load with acquire semantics at GPU scope: the writes another CTA made
+// before its release (a fence, then the update of this word) are visible to
+// this thread's later loads.
+__device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int *p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // L2 eviction-priority policies for the cache hints above.
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     uint64_t p;
