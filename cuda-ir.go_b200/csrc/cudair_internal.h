@@ -71,6 +71,9 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
                        int64_t ldb, int64_t ldc, int sm_count, unsigned int *status,
                        cudaStream_t stream);
 int skinny_reset_workspace();
+// The programmatic-dependent-launch mode of the few-row GEMM
+// (cudair_set_gemm_pdl): 0 off, 1 on, 2 on with B requested early.
+int gemm_pdl_mode();
 
 int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K,
                        int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t stream);

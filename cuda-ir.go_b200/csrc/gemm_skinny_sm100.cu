@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA,
                        float *__restrict__ C, int M, int N, int K, long long ldc, int mpad,
                        unsigned int *__restrict__ counters, float *__restrict__ partials,
-                       unsigned int *status) {
+                       unsigned int *status, int b_early) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -125,6 +125,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    // Every CTA is resident: the next kernel in the stream may be launched
+    // (it takes an SM when one of these CTAs exits).
+    if (threadIdx.x == 0) grid_launch_dependents();
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -133,7 +136,35 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t policy_a = l2_policy_evict_last();  // A is re-read by every CTA
             uint32_t stage = 0, phase = 0, issued = 0;
             bool ok = true;
-            for (long long x = r0; x < r1 && ok; ++x) {
+            long long x = r0;
+            if (b_early) {
+                // B does not depend on the preceding kernel (the caller's
+                // promise): the first ring of B boxes is requested before the
+                // dependency wait, A and the rest after it.
+                const long long pre_end = min(r1, r0 + static_cast<long long>(STAGES));
+                for (long long y = r0; y < pre_end; ++y) {
+                    const int t = static_cast<int>(y / num_kb), kb = static_cast<int>(y % num_kb);
+                    const int n0 = t * BN_T, k0 = kb * BK, s_ = static_cast<int>(y - r0);
+                    const int nb = (n0 + 64 < N) ? 2 : 1;
+                    mbar_arrive_expect_tx(&full[s_], nb * B_BOX_BYTES + a_stage_bytes);
+                    for (int j = 0; j < nb; ++j)
+                        tma_load_2d(sB + s_ * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB, &full[s_],
+                                    n0 + 64 * j, k0, policy_b);
+                }
+                grid_dependency_wait();
+                for (long long y = r0; y < pre_end; ++y) {
+                    const int s_ = static_cast<int>(y - r0);
+                    tma_load_2d(sA + s_ * a_stage_bytes, &tmA, &full[s_],
+                                static_cast<int>(y % num_kb) * BK, 0, policy_a);
+                }
+                issued = static_cast<uint32_t>(pre_end - r0);
+                stage = issued % static_cast<uint32_t>(STAGES);
+                phase = (issued == static_cast<uint32_t>(STAGES)) ? 1u : 0u;
+                x = pre_end;
+            } else {
+                grid_dependency_wait();
+            }
+            for (; x < r1 && ok; ++x) {
                 const int t = static_cast<int>(x / num_kb), kb = static_cast<int>(x % num_kb);
                 const int n0 = t * BN_T, k0 = kb * BK;
                 const int nb = (n0 + 64 < N) ? 2 : 1;  // skip a box wholly beyond N
@@ -217,6 +248,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
     } else {
         // ---------------- epilogue and fix-up (warps 2..5) ----------------
+        grid_dependency_wait();  // C and the workspace may be the preceding kernel's
         const uint32_t q = warp & 3u;
         const int nl = static_cast<int>(q * 32 + lane);  // n within the tile
         const bool leader = (warp == 2 && lane == 0);
@@ -390,6 +422,29 @@ int workspace(Workspace **out) {
 
 }  // namespace
 
+// Launches the few-row kernel.  pdl > 0 adds programmatic stream
+// serialization: the kernel may be launched while the preceding kernel in the
+// stream finishes, and waits on it (griddepcontrol.wait) before it reads A, C
+// or the workspace; pdl == 2 also lets it request B before that wait.
+cudaError_t launch_skinny(int grid, size_t smem, cudaStream_t stream, int pdl, const CUtensorMap &tmB,
+                          const CUtensorMap &tmA, float *c, int M, int N, int K, long long ldc, int mpad,
+                          unsigned int *counters, float *partials, unsigned int *status) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(skinny::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (pdl > 0) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, skinny::gemm_skinny_kernel, tmB, tmA, c, M, N, K, ldc, mpad, counters,
+                              partials, status, pdl == 2 ? 1 : 0);
+}
+
 // Called after a bounded wait gave up: a launch that unwound early may have
 // left tile counters raised, so they are zeroed before the next launch.
 int skinny_reset_workspace() {
@@ -440,9 +495,8 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
     const int grid = static_cast<int>(T < sm_count ? T : sm_count);
     unsigned int *counters = static_cast<unsigned int *>(ws->ptr);
     float *partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws->ptr) + skinny::COUNTER_BYTES);
-    skinny::gemm_skinny_kernel<<<grid, skinny::THREADS, skinny::smem_for(mpad), stream>>>(
-        tmB, tmA, c, M, N, K, static_cast<long long>(ldc), mpad, counters, partials, status);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_skinny(grid, skinny::smem_for(mpad), stream, gemm_pdl_mode(), tmB, tmA, c, M, N,
+                                  K, static_cast<long long>(ldc), mpad, counters, partials, status);
     if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch");
     return CUDAIR_OK;
 }
@@ -597,7 +651,7 @@ CUDAIR_API int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c
     cudaError_t e = cudaMemsetAsync(counters, 0, static_cast<size_t>(n_tiles) * sizeof(unsigned int), s);
     if (e != cudaSuccess) return cuda_error(e, "cudaMemsetAsync(no-alloc tile counters)");
     skinny::gemm_skinny_kernel<<<static_cast<unsigned>(grid), skinny::THREADS, skinny::smem_for(mpad), s>>>(
-        tmB, tmA, c, Mi, Ni, Ki, static_cast<long long>(ldc), mpad, counters, partials, status);
+        tmB, tmA, c, Mi, Ni, Ki, static_cast<long long>(ldc), mpad, counters, partials, status, 0);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch (no-alloc)");
     return CUDAIR_OK;

@@ -626,6 +626,7 @@ struct DeviceInfo {
 std::mutex g_dev_mu;
 DeviceInfo g_dev[64];
 std::atomic<int> g_variant{0};  // 0 auto, 1 single CTA, 2 CTA pair
+std::atomic<int> g_pdl{0};      // few-row GEMM: 0 plain launch, 1 PDL, 2 PDL with B early
 
 int device_info(DeviceInfo **out) {
     int dev = 0;
@@ -682,6 +683,8 @@ int device_info(DeviceInfo **out) {
 }
 
 }  // namespace
+
+int gemm_pdl_mode() { return g_pdl.load(); }
 
 int wait_status_current_device(unsigned int **status) {
     DeviceInfo *d = nullptr;
@@ -858,6 +861,15 @@ CUDAIR_API int cudair_set_gemm_variant(int variant) {
                          "3 (few rows) or 4 (CTA pair, 256 x 512 tiles)",
                          variant);
     g_variant.store(variant);
+    return CUDAIR_OK;
+}
+
+CUDAIR_API int cudair_set_gemm_pdl(int mode) {
+    clear_error();
+    if (mode < 0 || mode > 2)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm PDL mode %d, want 0 (off), 1 (on) or 2 (on, B read early)", mode);
+    g_pdl.store(mode);
     return CUDAIR_OK;
 }
 

@@ -163,6 +163,17 @@ __device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int *p
     return v;
 }
 
+// Programmatic dependent launch.  griddepcontrol.wait returns once the grids
+// this one depends on have completed and their memory is visible (at once
+// when the launch had no such dependency); launch_dependents lets the next
+// kernel in the stream be launched before this one ends.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // L2 eviction-priority policies for the cache hints above.
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     uint64_t p;

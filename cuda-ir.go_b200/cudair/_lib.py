@@ -41,6 +41,7 @@ SIGNATURES = {
     "cudair_gemm_f16f32_host": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                         c_vp, c_vp, c_vp, c_i64, c_vp]),
     "cudair_set_gemm_variant": (c_int, [c_int]),
+    "cudair_set_gemm_pdl": (c_int, [c_int]),
     "cudair_vecadd": (c_int, [c_vp, c_vp, c_vp, ctypes.c_int32, c_vp]),
     "cudair_reduce_f32": (c_int, [c_vp, c_vp, ctypes.c_int32, c_vp]),
     "cudair_wait_status": (c_int, [_u32p, c_int]),

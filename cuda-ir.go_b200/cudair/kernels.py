@@ -91,6 +91,12 @@ def set_gemm_variant(variant: int) -> None:
     check(lib().cudair_set_gemm_variant(variant))
 
 
+def set_gemm_pdl(mode: int) -> None:
+    """Programmatic dependent launch of the few-row GEMM: 0 off, 1 on, 2 on
+    with B (weights, not written by the preceding kernel) requested early."""
+    check(lib().cudair_set_gemm_pdl(mode))
+
+
 def vecadd(a, b, out, stream=None) -> None:
     """out = a + b over fp32 vectors (VecAdd's operands)."""
     import torch

@@ -171,6 +171,20 @@ int cudair_gemm_f16f32(const void *a, const void *b, float *c,
 int cudair_set_gemm_variant(int variant);
 
 /*
+ * Programmatic dependent launch for the few-row GEMM (M <= 64; the
+ * ProgrammaticStreamSerialization launch attribute of the reference's
+ * host.LaunchAttrs, host/launchex.go:105-148), for chains of GEMMs on one
+ * stream such as a decode step.  mode 0 (default): a plain launch.  mode 1:
+ * the launch may begin while the preceding kernel in the stream finishes; the
+ * kernel sets up and then waits for that kernel (griddepcontrol.wait) before
+ * it reads A, B, C or its workspace.  mode 2: as 1, but the first stages of B
+ * are requested before the wait.  The caller promises that the preceding
+ * kernel does not write B (weights).  Results are identical in all modes.
+ * Applies to subsequent calls of cudair_gemm_f16f32 in this process.
+ */
+int cudair_set_gemm_pdl(int mode);
+
+/*
  * C = A.B + C from host buffers: the flow of the reference's MatMul16 test
  * (advanced_test.go:466-483, which copies A, B and C to the device with
  * gocudrv CopyFrom, launches MatMul16 and copies C back with CopyTo) as one

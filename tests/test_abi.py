@@ -128,6 +128,14 @@ def test_gemm_host_empty_c_is_noop(cudair):
                                                     None, None, None, 0, None) == 0
 
 
+def test_gemm_pdl_mode_validation(cudair):
+    L = cudair.lib()
+    assert L.cudair_set_gemm_pdl(3) == 1 and "PDL mode 3" in cudair.last_error()
+    assert L.cudair_set_gemm_pdl(-1) == 1
+    for mode in (2, 1, 0):
+        assert L.cudair_set_gemm_pdl(mode) == 0
+
+
 def test_vecadd_and_reduce_validation(cudair):
     L = cudair.lib()
     assert L.cudair_vecadd(None, None, None, -1, None) == 1
