@@ -1,4 +1,4 @@
-// gemm_skinny_sm100.cu - the same C = A.B + C for few rows (M <= 64: the
+// gemm_skinny_sm100.cu - the same C = A.B + C for few rows (M <= 128: the
 // decode-shaped GEMM, e.g. M = 16, N = 14336, K = 4096), where the
 // square-tile kernels leave most SMs idle and the time is the one pass over
 // B (K x N fp16) through HBM.
@@ -16,10 +16,12 @@
 //     fp32 partials in a workspace, count themselves on the tile's counter,
 //     and the last to arrive adds C and the partials in CTA order (so the sum
 //     order, and the result, do not depend on timing), stores C and resets
-//     the counter to zero for the next launch.
+//     the counter to zero for the next launch.  The last contributor checks
+//     the counter first and, when it is last, adds its own part straight from
+//     TMEM without storing it.
 //   * a TMA ring of 16 KB B tiles (two 64 x 64 boxes) plus mpad x 64 A tiles,
-//     as many stages as fit (12 at M <= 16), keeps up to 216 KB of B in
-//     flight per SM.
+//     as many stages as fit (12 at M <= 16, 7 at M = 128), keeps up to
+//     192 KB of B in flight per SM.
 //
 // Roles as in gemm_sm100.cu (192 threads): warp 0 TMA producer, warp 1 TMEM
 // owner and MMA issuer, warps 2-5 epilogue and fix-up.  All waits are
@@ -40,14 +42,15 @@ constexpr int BN_T = 128;  // n per tile (the MMA's M)
 constexpr int BK = 64;
 constexpr int MAX_STAGES = 12;
 constexpr int THREADS = 192;
-constexpr int MAX_M = 64;
+constexpr int MAX_M = 128;
 constexpr uint32_t B_BOX_BYTES = 64 * BK * 2;        // 64 n x 64 k
 constexpr uint32_t B_STAGE_BYTES = 2 * B_BOX_BYTES;  // 16 KB
 constexpr uint32_t BAR_BYTES = 256;
 constexpr size_t SMEM_BYTES = 227 * 1024;  // the launch's dynamic shared memory limit
 
 // The ring holds as many stages of (B tile + this M's A tile) as fit: with
-// M <= 16 that is 12 stages (216 KB of B in flight per SM), with M = 64 nine.
+// M <= 16 that is 12 stages (192 KB of B in flight per SM), with M = 64 nine,
+// with M = 128 seven.
 __host__ __device__ constexpr int stages_for(int mpad) {
     return static_cast<int>((SMEM_BYTES - 1024 - BAR_BYTES) / (B_STAGE_BYTES + mpad * BK * 2)) < MAX_STAGES
                ? static_cast<int>((SMEM_BYTES - 1024 - BAR_BYTES) / (B_STAGE_BYTES + mpad * BK * 2))
@@ -56,7 +59,7 @@ __host__ __device__ constexpr int stages_for(int mpad) {
 __host__ __device__ constexpr size_t smem_for(int mpad) {
     return 1024 + static_cast<size_t>(stages_for(mpad)) * (B_STAGE_BYTES + mpad * BK * 2) + BAR_BYTES;
 }
-static_assert(smem_for(16) <= SMEM_BYTES && smem_for(64) <= SMEM_BYTES, "shared memory budget");
+static_assert(smem_for(16) <= SMEM_BYTES && smem_for(MAX_M) <= SMEM_BYTES, "shared memory budget");
 static_assert(2 * MAX_STAGES * 8 + 5 * 8 + 12 <= BAR_BYTES, "barrier area");
 
 // Workspace layout: tile counters first, then two partial slots per CTA.
@@ -100,7 +103,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int G = static_cast<int>(gridDim.x);
     const int c = static_cast<int>(blockIdx.x);
     const long long r0 = range_start(c, T, G), r1 = range_start(c + 1, T, G);
-    const uint32_t tmem_cols = mpad <= 16 ? 32u : (mpad <= 32 ? 64u : 128u);
+    const uint32_t tmem_cols = mpad <= 16 ? 32u : (mpad <= 32 ? 64u : (mpad <= 64 ? 128u : 256u));
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -268,25 +271,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             named_bar_sync(1, 128);
             if (!ok || *abort_flag) break;
             tc_fence_after_sync();
-            // This thread's column of the accumulator (row m of C in own[m]).
+            // This thread's column of the accumulator, read from TMEM sixteen
+            // rows at a time wherever it is needed; the accumulator is handed
+            // back only after the tile is done.
             const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * static_cast<uint32_t>(mpad);
-            uint32_t own[MAX_M];
-#pragma unroll
-            for (int j = 0; j < MAX_M / 16; ++j)
-                if (16 * j < mpad)
-                    tmem_ld_32x32b_x16(t_row + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(own + 16 * j));
-            tmem_ld_wait();
-            tc_fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[acc]);
-            acc ^= 1u;
-            if (acc == 0) acc_phase ^= 1u;
-
+            const int chunks = mpad / 16;
             if (whole) {
-                if (n < N) {
-#pragma unroll
-                    for (int j = 0; j < MAX_M / 16; ++j) {
-                        if (16 * j >= M) break;
+                for (int j = 0; j < chunks; ++j) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(t_row + 16 * j, r);
+                    tmem_ld_wait();
+                    if (n < N) {
                         float v[16];
 #pragma unroll
                         for (int i = 0; i < 16; ++i)
@@ -294,80 +289,92 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                         for (int i = 0; i < 16; ++i)
                             if (16 * j + i < M)
-                                C[static_cast<long long>(16 * j + i) * ldc + n] = v[i] + __uint_as_float(own[16 * j + i]);
+                                C[static_cast<long long>(16 * j + i) * ldc + n] = v[i] + __uint_as_float(r[i]);
                     }
                 }
-                continue;
-            }
-
-            // Partial tile.  Contributors c_lo .. c_hi; the one that finishes
-            // last adds C and every contributor's part in CTA order (so the
-            // result does not depend on timing) and resets the tile counter.
-            // Each other contributor writes its part to the workspace, makes
-            // it visible and counts itself in.  A contributor that finds all
-            // the others counted in already is last without writing its part.
-            const int c_lo = cta_of(tile_lo, T, G), c_hi = cta_of(tile_hi - 1, T, G);
-            const unsigned int others = static_cast<unsigned int>(c_hi - c_lo);
-            if (leader) *last_flag = (ld_acquire_gpu_u32(&counters[t]) == others) ? 1 : 0;
-            named_bar_sync(1, 128);
-            bool last = *last_flag != 0;
-            if (!last) {
-                float *part = partials + (static_cast<size_t>(c) * 2 + slot) * BN_T * mpad;
-#pragma unroll
-                for (int m = 0; m < MAX_M; ++m)
-                    if (m < mpad) part[m * BN_T + nl] = __uint_as_float(own[m]);
-                __threadfence();
+            } else {
+                // Partial tile.  Contributors c_lo .. c_hi; the one that
+                // finishes last adds C and every contributor's part in CTA
+                // order (so the result does not depend on timing) and resets
+                // the tile counter.  Each other contributor writes its part to
+                // the workspace, makes it visible and counts itself in.  A
+                // contributor that finds all the others counted in already is
+                // last without writing its part.
+                const int c_lo = cta_of(tile_lo, T, G), c_hi = cta_of(tile_hi - 1, T, G);
+                const unsigned int others = static_cast<unsigned int>(c_hi - c_lo);
+                if (leader) *last_flag = (ld_acquire_gpu_u32(&counters[t]) == others) ? 1 : 0;
                 named_bar_sync(1, 128);
-                if (leader) {
-                    const unsigned int prev = atomicAdd(&counters[t], 1u);
-                    *last_flag = (prev == others) ? 1 : 0;
+                bool last = *last_flag != 0;
+                if (!last) {
+                    float *part = partials + (static_cast<size_t>(c) * 2 + slot) * BN_T * mpad;
+                    for (int j = 0; j < chunks; ++j) {
+                        uint32_t r[16];
+                        tmem_ld_32x32b_x16(t_row + 16 * j, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) part[(16 * j + i) * BN_T + nl] = __uint_as_float(r[i]);
+                    }
+                    __threadfence();
+                    named_bar_sync(1, 128);
+                    if (leader) {
+                        const unsigned int prev = atomicAdd(&counters[t], 1u);
+                        *last_flag = (prev == others) ? 1 : 0;
+                    }
+                    named_bar_sync(1, 128);
+                    last = *last_flag != 0;
                 }
-                named_bar_sync(1, 128);
-                last = *last_flag != 0;
-            }
-            if (last) {
-                __threadfence();
-                // Sixteen rows at a time: C and up to four contributors'
-                // parts are loaded together (one memory latency per four
-                // contributors), then added in contributor order.
-                if (n < N) {
-#pragma unroll
-                    for (int j = 0; j < MAX_M / 16; ++j) {
+                if (last) {
+                    __threadfence();
+                    // Sixteen rows at a time: this CTA's part from TMEM, C and
+                    // up to four other contributors' parts loaded together
+                    // (one memory latency per four contributors), then added
+                    // in contributor order.
+                    for (int j = 0; j < chunks; ++j) {
                         if (16 * j >= M) break;
-                        float v[16];
+                        uint32_t r[16];
+                        tmem_ld_32x32b_x16(t_row + 16 * j, r);
+                        tmem_ld_wait();
+                        if (n < N) {
+                            float v[16];
 #pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            v[i] = (16 * j + i < M) ? C[static_cast<long long>(16 * j + i) * ldc + n] : 0.f;
-                        for (int cb = c_lo; cb <= c_hi; cb += 4) {
-                            float pv[4][16];
+                            for (int i = 0; i < 16; ++i)
+                                v[i] = (16 * j + i < M) ? C[static_cast<long long>(16 * j + i) * ldc + n] : 0.f;
+                            for (int cb = c_lo; cb <= c_hi; cb += 4) {
+                                float pv[4][16];
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const int cc = cb + k;
-                                if (cc > c_hi || cc == c) continue;
-                                const long long s_cc = range_start(cc, T, G);
-                                const int sl = (s_cc / num_kb == t) ? 0 : 1;
-                                const float *pc = partials + (static_cast<size_t>(cc) * 2 + sl) * BN_T * mpad;
+                                for (int k = 0; k < 4; ++k) {
+                                    const int cc = cb + k;
+                                    if (cc > c_hi || cc == c) continue;
+                                    const long long s_cc = range_start(cc, T, G);
+                                    const int sl = (s_cc / num_kb == t) ? 0 : 1;
+                                    const float *pc = partials + (static_cast<size_t>(cc) * 2 + sl) * BN_T * mpad;
 #pragma unroll
-                                for (int i = 0; i < 16; ++i)
-                                    pv[k][i] = (16 * j + i < M) ? __ldcg(pc + (16 * j + i) * BN_T + nl) : 0.f;
+                                    for (int i = 0; i < 16; ++i)
+                                        pv[k][i] = (16 * j + i < M) ? __ldcg(pc + (16 * j + i) * BN_T + nl) : 0.f;
+                                }
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    const int cc = cb + k;
+                                    if (cc > c_hi) break;
+#pragma unroll
+                                    for (int i = 0; i < 16; ++i)
+                                        v[i] += (cc == c) ? __uint_as_float(r[i]) : pv[k][i];
+                                }
                             }
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const int cc = cb + k;
-                                if (cc > c_hi) break;
-#pragma unroll
-                                for (int i = 0; i < 16; ++i)
-                                    v[i] += (cc == c) ? __uint_as_float(own[16 * j + i]) : pv[k][i];
-                            }
+                            for (int i = 0; i < 16; ++i)
+                                if (16 * j + i < M) C[static_cast<long long>(16 * j + i) * ldc + n] = v[i];
                         }
-#pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            if (16 * j + i < M) C[static_cast<long long>(16 * j + i) * ldc + n] = v[i];
                     }
+                    if (leader) counters[t] = 0u;
                 }
-                if (leader) counters[t] = 0u;
+                named_bar_sync(1, 128);  // last_flag is reused by the next partial tile
             }
-            named_bar_sync(1, 128);  // last_flag is reused by the next partial tile
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
         }
         __syncwarp();
     }
@@ -392,7 +399,10 @@ struct Workspace {
 std::mutex g_ws_mu;
 Workspace g_ws[64];
 
-constexpr size_t kWorkspaceBytes = 16u << 20;
+// Tile counters, then two partial slots (128 x M fp32) per CTA for up to 160
+// CTAs at M = 128: 21.25 MB.
+constexpr size_t kWorkspaceBytes =
+    skinny::COUNTER_BYTES + 160u * 2u * skinny::BN_T * skinny::MAX_M * sizeof(float);
 
 // The library's per-device workspace of the skinny kernel (tile counters +
 // partial slots), allocated and zeroed on the first call on a device.
@@ -492,7 +502,12 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
         if (rc != CUDAIR_OK) return rc;
     }
     const long long T = static_cast<long long>(n_tiles) * ((K + skinny::BK - 1) / skinny::BK);
-    const int grid = static_cast<int>(T < sm_count ? T : sm_count);
+    // One CTA per SM, as many as there are units and as the partial slots hold.
+    const long long slots_fit = static_cast<long long>(ws->bytes - skinny::COUNTER_BYTES) /
+                                (2LL * skinny::BN_T * mpad * static_cast<long long>(sizeof(float)));
+    long long g = T < sm_count ? T : sm_count;
+    if (g > slots_fit) g = slots_fit;
+    const int grid = static_cast<int>(g);
     unsigned int *counters = static_cast<unsigned int *>(ws->ptr);
     float *partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws->ptr) + skinny::COUNTER_BYTES);
     cudaError_t e = launch_skinny(grid, skinny::smem_for(mpad), stream, gemm_pdl_mode(), tmB, tmA, c, M, N,
@@ -510,7 +525,7 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
 // is owned end to end by another allocator (a framework's caching allocator,
 // or a pool reserved at start-up), or allocation is forbidden once they are
 // serving, because cudaMalloc may synchronise the device and stall every
-// other stream.  cudair_gemm_f16f32 allocates the few-row kernel's 16 MB
+// other stream.  cudair_gemm_f16f32 allocates the few-row kernel's 21 MB
 // workspace on its first call on a device; this entry point instead keeps
 // that scratch space in a fixed array in the library's own device memory,
 // reserved when the library is loaded, so no call ever allocates.
@@ -521,6 +536,7 @@ namespace {
 // Tile counters for up to 4096 n-tiles (N <= 524288), then 4 MiB of partial
 // sums: 4 MiB + 16 KiB in all.
 constexpr int kNoAllocMaxTiles = 4096;
+constexpr int kNoAllocMaxM = 64;
 constexpr size_t kNoAllocCounterBytes = kNoAllocMaxTiles * sizeof(unsigned int);
 constexpr size_t kNoAllocPartialBytes = 4u << 20;
 }  // namespace
@@ -585,10 +601,10 @@ CUDAIR_API int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_noalloc: negative size M=%lld N=%lld K=%lld",
                          (long long)M, (long long)N, (long long)K);
     if (M == 0 || N == 0 || K == 0) return CUDAIR_OK;  // C = C
-    if (M > skinny::MAX_M)
+    if (M > kNoAllocMaxM)
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm_noalloc: M = %lld exceeds the maximum of %d rows", (long long)M,
-                         skinny::MAX_M);
+                         kNoAllocMaxM);
     if (N > static_cast<int64_t>(kNoAllocMaxTiles) * skinny::BN_T)
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm_noalloc: N = %lld exceeds the maximum of %d columns", (long long)N,

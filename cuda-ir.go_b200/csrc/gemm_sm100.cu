@@ -80,7 +80,10 @@ constexpr size_t S_SMEM = 1024 + S_STAGES * (A_BOX_BYTES + S_STAGE_B) + EPI_BYTE
 // tiles, two accumulators; NB = 2: 256 x 512 tiles, one accumulator filling
 // TMEM, a quarter fewer operand bytes per FLOP).
 constexpr int P_BM = 256;  // rows per pair tile, 128 per CTA
-constexpr int P_GROUP_M = 8;
+#ifndef CUDAIR_P_GROUP_M
+#define CUDAIR_P_GROUP_M 8
+#endif
+constexpr int P_GROUP_M = CUDAIR_P_GROUP_M;
 template <int NB>
 struct PairCfg {
     static constexpr int TILE_N = 256 * NB;
@@ -747,7 +750,13 @@ int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_
     if (rc != CUDAIR_OK) return rc;
 
     const int variant = g_variant.load();
-    if (variant == 3 || (variant == 0 && M <= 64))
+    // The few-row (stream-K) kernel takes M <= 64, and 64 < M <= 128 up to
+    // N = 8192.  Past that its re-reads of A from L2 (one per 128-column
+    // tile) cost more than the single-CTA kernel's idle SMs (measured: at
+    // M = 128, K = 8192: 51.0 against 54.6 us for N = 8192; at K = 4096,
+    // 47.5 against 33.2 us for N = 14336).
+    const bool fewrows_auto = variant == 0 && (M <= 64 || (M <= 128 && N <= 8192));
+    if (variant == 3 || fewrows_auto)
         return gemm_skinny_launch(a, b, c, static_cast<int>(M), static_cast<int>(N),
                                   static_cast<int>(K), lda, ldb, ldc, dev->sm_count, dev->status,
                                   stream);

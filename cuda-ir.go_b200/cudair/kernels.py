@@ -87,7 +87,7 @@ def gemm_host(a_h, b_h, c_h, a_d, b_d, c_d, rows_per_block=0, stream=None) -> No
 
 def set_gemm_variant(variant: int) -> None:
     """0 = automatic, 1 = single-CTA 128x256 tiles, 2 = CTA-pair 256x256 tiles,
-    3 = few-row kernel (M <= 64), 4 = CTA-pair 256x512 tiles."""
+    3 = few-row kernel (M <= 128), 4 = CTA-pair 256x512 tiles."""
     check(lib().cudair_set_gemm_variant(variant))
 
 

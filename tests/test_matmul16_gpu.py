@@ -36,7 +36,7 @@ def no_wait_timeouts(dev, cudair):
 @pytest.fixture(params=[1, 2, 3, 4], ids=["single", "pair", "fewrows", "pairwide"])
 def variant(request, dev, cudair):
     """Runs a test on each GEMM kernel in turn: single CTA (128x256 tiles),
-    CTA pair (256x256), the few-row kernel (M <= 64) and the wide CTA pair
+    CTA pair (256x256), the few-row kernel (M <= 128) and the wide CTA pair
     (256x512), then restores the automatic choice."""
     from cudair import kernels
     kernels.set_gemm_variant(request.param)
@@ -45,8 +45,8 @@ def variant(request, dev, cudair):
 
 
 def _applies(variant, M):
-    if variant == 3 and M > 64:
-        pytest.skip("the few-row kernel takes M <= 64")
+    if variant == 3 and M > 128:
+        pytest.skip("the few-row kernel takes M <= 128")
 
 
 def kat(M, N, K):
@@ -151,6 +151,7 @@ def test_matmul16_tcgen05_seeded_n256(dev, cudair, oracle, golden_dir):
     (1, 8, 8), (7, 16, 24), (128, 256, 64), (129, 264, 72), (200, 264, 136), (300, 1000, 1000),
     (513, 8, 4096), (16, 14336, 512), (1000, 2056, 520), (257, 136, 64), (384, 384, 8),
     (5, 136, 200), (33, 1000, 1000), (64, 2048, 8), (48, 520, 4104), (17, 128, 64),
+    (65, 1000, 1032), (96, 2056, 520), (128, 4096, 2048), (113, 264, 8192),
 ])
 def test_gemm_tcgen05_ragged_kat_exact(dev, cudair, variant, M, N, K):
     import torch
@@ -253,7 +254,8 @@ def test_gemm_repeated_calls_accumulate(dev, cudair, variant, M):
     assert np.array_equal(dc.cpu().numpy(), want2)
 
 
-@pytest.mark.parametrize("M,N,K", [(16, 14336, 4096), (3, 4096, 12288), (64, 1024, 520)])
+@pytest.mark.parametrize("M,N,K", [(16, 14336, 4096), (3, 4096, 12288), (64, 1024, 520),
+                                   (128, 8192, 2048), (100, 1000, 4104)])
 def test_fewrows_deterministic_and_within_tolerance(dev, cudair, oracle, M, N, K):
     # The split-K fix-up sums partials in a fixed order: two runs from the
     # same C give identical bits, and both match the oracle within tolerance.
