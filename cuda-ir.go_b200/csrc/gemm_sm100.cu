@@ -49,6 +49,8 @@
 #include <atomic>
 #include <mutex>
 
+#include <cuda_fp16.h>
+
 #include "cudair_internal.h"
 #include "sm100.cuh"
 
@@ -125,39 +127,70 @@ __device__ __forceinline__ uint64_t c_policy() {
     return p;
 }
 
-// Adds this warp's 32 accumulator rows (TMEM lanes from t_row, 256 columns)
-// into C with TMA reduce-add.  Each 32-column chunk goes TMEM -> registers ->
-// a 32 x 32 staging box in shared memory (the 128-byte swizzled layout of
-// tmC, so the row-per-thread stores are free of bank conflicts) -> one
-// cp.reduce.async.bulk.tensor, and L2 adds the box into C: C never enters the
-// SM, and each element of C gets exactly one add, C + (A.B), rounded once.
+// How the epilogue writes the accumulator into C.
+enum Epilogue : int {
+    kEpiScalarAdd = 0,  // C += acc, fp32, element by element (C not 16-byte aligned)
+    kEpiReduceF32 = 1,  // C += acc, fp32, TMA reduce-add in L2
+    kEpiStoreF32 = 2,   // C = acc, fp32, TMA store
+    kEpiStoreF16 = 3,   // C = acc rounded to fp16, TMA store
+};
+
+// Writes this warp's 32 accumulator rows (TMEM lanes from t_row, 256 columns)
+// into C through TMA.  Each chunk goes TMEM -> registers -> a 4 KB staging box
+// in shared memory (the 128-byte swizzled layout of tmC, so the
+// row-per-thread stores are free of bank conflicts) -> one bulk tensor copy:
+//   kEpiReduceF32: 32 x 32 fp32 boxes through cp.reduce.async.bulk.tensor, so
+//     L2 adds the box into C: C never enters the SM, and each element of C
+//     gets exactly one add, C + (A.B), rounded once;
+//   kEpiStoreF32: the same boxes stored (C = A.B);
+//   kEpiStoreF16: 32 x 64 boxes rounded to fp16 (round to nearest) and stored.
 // Rows and columns outside C are clipped by the tensor map.  The warp's two
 // boxes alternate (`buf` carries over between calls); lane 0 issues and
-// tracks the bulk groups, and a box is rewritten only after the reduce that
+// tracks the bulk groups, and a box is rewritten only after the copy that
 // last read it has finished reading.
-__device__ __forceinline__ void epilogue_rows_reduce(uint32_t t_row, const CUtensorMap *tmC,
-                                                     uint32_t boxes, int row0, int n0, int N,
-                                                     uint64_t pol, uint32_t &buf) {
+__device__ __forceinline__ void epilogue_rows_tma(uint32_t t_row, const CUtensorMap *tmC,
+                                                  uint32_t boxes, int row0, int n0, int N,
+                                                  uint64_t pol, uint32_t &buf, int epi) {
     const uint32_t lane = lane_id();
+    const int width = (epi == kEpiStoreF16) ? 64 : 32;  // columns per box
 #pragma unroll 1
-    for (int ch = 0; ch < BN / 32; ++ch) {
-        const int col = n0 + ch * 32;
+    for (int col0 = 0; col0 < BN; col0 += width) {
+        const int col = n0 + col0;
         if (col >= N) break;  // the rest of the block lies beyond C
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + ch * 32, r);
+        uint32_t r[32], r2[32];
+        tmem_ld_32x32b_x32(t_row + col0, r);
+        if (epi == kEpiStoreF16) tmem_ld_32x32b_x32(t_row + col0 + 32, r2);
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
         tmem_ld_wait();
         const uint32_t box = boxes + buf * EPI_BOX_BYTES;
         const uint32_t row_addr = box + lane * 128u;
+        if (epi == kEpiStoreF16) {
+            uint32_t h[32];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            st_shared_v4(row_addr + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4), r[4 * j],
-                         r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            for (int k = 0; k < 16; ++k) {
+                const __half2 lo = __floats2half2_rn(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+                const __half2 hi = __floats2half2_rn(__uint_as_float(r2[2 * k]), __uint_as_float(r2[2 * k + 1]));
+                h[k] = *reinterpret_cast<const uint32_t *>(&lo);
+                h[16 + k] = *reinterpret_cast<const uint32_t *>(&hi);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                st_shared_v4(row_addr + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4), h[4 * j],
+                             h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                st_shared_v4(row_addr + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4), r[4 * j],
+                             r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-            tma_reduce_add_2d(tmC, box, col, row0, pol);
+            if (epi == kEpiReduceF32)
+                tma_reduce_add_2d(tmC, box, col, row0, pol);
+            else
+                tma_store_2d(tmC, box, col, row0, pol);
             bulk_commit_group();
         }
         buf ^= 1u;
@@ -182,13 +215,16 @@ __device__ __forceinline__ void epilogue_rows_scalar(uint32_t t_row, float *crow
 }
 
 // =============================================================================
-// Single-CTA variant: 128 x 256 tiles.
+// Single-CTA variant: 128 x 256 tiles.  BT: B is stored transposed (N x K,
+// K-major) instead of K x N.  idesc: the MMA's instruction descriptor (fp16
+// or bf16 operands); epi: an Epilogue mode.
 // =============================================================================
+template <bool BT>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16f32_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, float *__restrict__ C, int M,
-                       int N, int K, long long ldc, int reduce) {
+                       int N, int K, long long ldc, uint32_t idesc, int epi) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // 1024-aligned tiles
@@ -226,7 +262,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_mbar_init();
         tma_prefetch_map(&tmA);
         tma_prefetch_map(&tmB);
-        if (reduce) tma_prefetch_map(&tmC);
+        if (epi != kEpiScalarAdd) tma_prefetch_map(&tmC);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, TMEM_COLS);
@@ -260,9 +296,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mbar_arrive_expect_tx(&full[stage], tx);
                     const int k0 = kb * BK;
                     tma_load_2d(sA + stage * A_BOX_BYTES, &tmA, &full[stage], k0, m0, policy);
+                    // 64-column B boxes: (n, k) for B as stored, (k, n) for B^T.
                     for (int j = 0; j < nb; ++j)
                         tma_load_2d(sB + stage * S_STAGE_B + j * B_BOX_BYTES, &tmB, &full[stage],
-                                    n0 + 64 * j, k0, policy);
+                                    BT ? k0 : n0 + 64 * j, BT ? n0 + 64 * j : k0, policy);
                     ++issued;
                     if (++stage == S_STAGES) {
                         stage = 0;
@@ -283,7 +320,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(S_BM, BN, false, true);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true, issued_any = false;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -306,9 +342,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         // A: K-major rows of 128 B; +32 B per 16-wide k step.
                         const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
-                        // B: MN-major; 16 k-rows of 128 B per k step, n-blocks 8 KB apart.
+                        // B as stored: MN-major, 16 k-rows of 128 B per k step, n-blocks
+                        // 8 KB apart.  B^T: K-major like A.
                         const uint64_t b_desc =
-                            smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
+                            BT ? smem_desc_sw128(b_base + kk * 32, 16, 1024)
+                               : smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
                         umma_f16_ss(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
                     }
                     issued_any = true;
@@ -344,8 +382,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 break;
             tc_fence_after_sync();
             const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
-            if (reduce) {
-                if (row0 < M) epilogue_rows_reduce(t_row, &tmC, boxes, row0, n0, N, cpol, buf);
+            if (epi != kEpiScalarAdd) {
+                if (row0 < M) epilogue_rows_tma(t_row, &tmC, boxes, row0, n0, N, cpol, buf, epi);
             } else {
                 const int row = row0 + static_cast<int>(lane);
                 epilogue_rows_scalar(t_row, C + static_cast<long long>(row) * ldc, row, n0, M, N);
@@ -373,12 +411,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 // =============================================================================
 // CTA-pair variants: clusters of 2, 256 x (256 NB) tiles, cta_group::2.
 // =============================================================================
-template <int NB>
+template <int NB, bool BT>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16f32_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                             const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmC, float *__restrict__ C, int M,
-                            int N, int K, long long ldc, int reduce) {
+                            int N, int K, long long ldc, uint32_t idesc, int epi) {
     using Cfg = PairCfg<NB>;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -423,7 +461,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_mbar_init();
         tma_prefetch_map(&tmA);
         tma_prefetch_map(&tmB);
-        if (reduce) tma_prefetch_map(&tmC);
+        if (epi != kEpiScalarAdd) tma_prefetch_map(&tmC);
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -477,9 +515,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int h = 0; h < NB; ++h) {
                         const int n_mine = n_pair + 256 * h + 128 * static_cast<int>(rank);
                         const int nb_mine = boxes(n_mine);
+                        // 64-column B boxes: (n, k) for B as stored, (k, n) for B^T.
                         for (int j = 0; j < nb_mine; ++j)
                             tma_load_2d_pair(sB + stage * Cfg::STAGE_B + (2 * h + j) * B_BOX_BYTES,
-                                             &tmB, full_even, n_mine + 64 * j, k0, policy);
+                                             &tmB, full_even, BT ? k0 : n_mine + 64 * j,
+                                             BT ? n_mine + 64 * j : k0, policy);
                     }
                     if (++stage == STAGES) {
                         stage = 0;
@@ -497,7 +537,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (even CTA) ----------------
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(P_BM, 256, false, true);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true, issued_any = false;
             for (int t = cluster; t < num_tiles && ok; t += num_clusters) {
@@ -523,8 +562,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
 #pragma unroll
                         for (int h = 0; h < NB; ++h) {
-                            const uint64_t b_desc = smem_desc_sw128(
-                                b_base + h * 2 * B_BOX_BYTES + kk * 2048, B_BOX_BYTES, 1024);
+                            const uint32_t b_blk = b_base + h * 2 * B_BOX_BYTES;
+                            const uint64_t b_desc =
+                                BT ? smem_desc_sw128(b_blk + kk * 32, 16, 1024)
+                                   : smem_desc_sw128(b_blk + kk * 2048, B_BOX_BYTES, 1024);
                             umma_f16_ss_pair(d_tmem + h * 256, a_desc, b_desc, idesc,
                                              (kb | kk) != 0 ? 1u : 0u);
                         }
@@ -567,10 +608,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * 256;
 #pragma unroll 1
             for (int h = 0; h < NB; ++h) {
-                if (reduce) {
+                if (epi != kEpiScalarAdd) {
                     if (row0 < M)
-                        epilogue_rows_reduce(t_row + 256 * h, &tmC, boxes, row0, n0 + 256 * h, N,
-                                             cpol, buf);
+                        epilogue_rows_tma(t_row + 256 * h, &tmC, boxes, row0, n0 + 256 * h, N, cpol,
+                                          buf, epi);
                 } else {
                     const int row = row0 + static_cast<int>(lane);
                     epilogue_rows_scalar(t_row + 256 * h, C + static_cast<long long>(row) * ldc, row,
@@ -649,17 +690,22 @@ int device_info(DeviceInfo **out) {
                          "cudair: device %d has compute capability %d.%d; this build targets sm_100a",
                          dev, d.major, d.minor);
     if (!d.attr_set) {
-        e = cudaFuncSetAttribute(gemm::gemm_f16f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(gemm::S_SMEM));
-        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(single)");
-        e = cudaFuncSetAttribute(gemm::gemm_f16f32_pair_kernel<1>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(gemm::PairCfg<1>::SMEM));
-        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(pair)");
-        e = cudaFuncSetAttribute(gemm::gemm_f16f32_pair_kernel<2>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(gemm::PairCfg<2>::SMEM));
-        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(pair, wide)");
+        const struct {
+            const void *fn;
+            size_t smem;
+        } kernels[] = {
+            {reinterpret_cast<const void *>(gemm::gemm_f16f32_kernel<false>), gemm::S_SMEM},
+            {reinterpret_cast<const void *>(gemm::gemm_f16f32_kernel<true>), gemm::S_SMEM},
+            {reinterpret_cast<const void *>(gemm::gemm_f16f32_pair_kernel<1, false>), gemm::PairCfg<1>::SMEM},
+            {reinterpret_cast<const void *>(gemm::gemm_f16f32_pair_kernel<1, true>), gemm::PairCfg<1>::SMEM},
+            {reinterpret_cast<const void *>(gemm::gemm_f16f32_pair_kernel<2, false>), gemm::PairCfg<2>::SMEM},
+            {reinterpret_cast<const void *>(gemm::gemm_f16f32_pair_kernel<2, true>), gemm::PairCfg<2>::SMEM},
+        };
+        for (const auto &k : kernels) {
+            e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(k.smem));
+            if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
+        }
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -672,7 +718,7 @@ int device_info(DeviceInfo **out) {
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         int clusters = 0;
-        e = cudaOccupancyMaxActiveClusters(&clusters, gemm::gemm_f16f32_pair_kernel<1>, &cfg);
+        e = cudaOccupancyMaxActiveClusters(&clusters, gemm::gemm_f16f32_pair_kernel<1, false>, &cfg);
         if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveClusters");
         d.max_pairs = clusters;
         void *sym = nullptr;
@@ -723,123 +769,188 @@ int auto_pair_nb(int64_t M, int64_t N, int64_t K, int pairs) {
 }
 }  // namespace gemm
 
-int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K,
-                       int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t stream) {
+namespace {
+
+// Launches one square-tile kernel instance: the single-CTA kernel (nb = 0) or
+// the CTA-pair kernel with nb 256-column blocks per tile.
+template <bool BT>
+cudaError_t launch_square(int nb, const DeviceInfo &dev, const CUtensorMap &tmA, const CUtensorMap &tmB,
+                          const CUtensorMap &tmC, float *c, int64_t M, int64_t N, int64_t K,
+                          long long ldc, bool bf16, int epi, cudaStream_t stream) {
+    const int Mi = static_cast<int>(M), Ni = static_cast<int>(N), Ki = static_cast<int>(K);
+    if (nb == 0) {
+        const int64_t tiles = ((M + gemm::S_BM - 1) / gemm::S_BM) * ((N + gemm::BN - 1) / gemm::BN);
+        const int grid = static_cast<int>(tiles < dev.sm_count ? tiles : dev.sm_count);
+        const uint32_t idesc = idesc_f16_f32(gemm::S_BM, gemm::BN, false, !BT, bf16);
+        gemm::gemm_f16f32_kernel<BT><<<grid, gemm::THREADS, gemm::S_SMEM, stream>>>(
+            tmA, tmB, tmC, c, Mi, Ni, Ki, ldc, idesc, epi);
+        return cudaGetLastError();
+    }
+    const int tile_n = 256 * nb;
+    const int64_t tiles = ((M + gemm::P_BM - 1) / gemm::P_BM) * ((N + tile_n - 1) / tile_n);
+    const int pairs = static_cast<int>(tiles < dev.max_pairs ? tiles : dev.max_pairs);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(gemm::THREADS, 1, 1);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const uint32_t idesc = idesc_f16_f32(gemm::P_BM, 256, false, !BT, bf16);
+    if (nb == 2) {
+        cfg.dynamicSmemBytes = gemm::PairCfg<2>::SMEM;
+        return cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<2, BT>, tmA, tmB, tmC, c, Mi, Ni, Ki,
+                                  ldc, idesc, epi);
+    }
+    cfg.dynamicSmemBytes = gemm::PairCfg<1>::SMEM;
+    return cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<1, BT>, tmA, tmB, tmC, c, Mi, Ni, Ki,
+                              ldc, idesc, epi);
+}
+
+}  // namespace
+
+// The argument rules of the GEMM entry points; CUDAIR_OK when the call is
+// valid (including the no-op sizes).
+int gemm_check(const void *a, const void *b, const void *c, int64_t M, int64_t N, int64_t K, int64_t lda,
+               int64_t ldb, int64_t ldc, uint32_t flags) {
+    constexpr uint32_t kKnown = CUDAIR_GEMM_BF16 | CUDAIR_GEMM_B_T | CUDAIR_GEMM_OVERWRITE | CUDAIR_GEMM_C_F16;
+    if (flags & ~kKnown) return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: unknown flags 0x%x", flags);
+    const bool bt = flags & CUDAIR_GEMM_B_T;
+    const bool overwrite = flags & CUDAIR_GEMM_OVERWRITE, c_f16 = flags & CUDAIR_GEMM_C_F16;
+    if (c_f16 && !overwrite)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: a half C is written, not accumulated into: "
+                                             "CUDAIR_GEMM_C_F16 needs CUDAIR_GEMM_OVERWRITE");
     if (M < 0 || N < 0 || K < 0)
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: negative size M=%lld N=%lld K=%lld",
                          (long long)M, (long long)N, (long long)K);
-    if (M == 0 || N == 0 || K == 0) return CUDAIR_OK;  // C = C
+    if (M == 0 || N == 0 || (K == 0 && !overwrite)) return CUDAIR_OK;  // C = C
     if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: sizes must fit int32");
-    if (!a || !b || !c) return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: nil pointer");
-    if (lda < K || ldb < N || ldc < N)
+    if (!c) return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: nil pointer");
+    if (ldc < N)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: leading dimension ldc=%lld too small",
+                         (long long)ldc);
+    // With K = 0 nothing of A or B is read (a written C becomes zero), so
+    // their pointers and pitches are not checked.
+    if (K > 0) {
+        if (!a || !b) return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: nil pointer");
+        if (lda < K || ldb < (bt ? K : N))
+            return set_error(CUDAIR_ERR_INVALID,
+                             "cudair: gemm: leading dimensions lda=%lld ldb=%lld ldc=%lld too small",
+                             (long long)lda, (long long)ldb, (long long)ldc);
+        if (lda % 8 || ldb % 8)
+            return set_error(CUDAIR_ERR_INVALID,
+                             "cudair: gemm: lda=%lld and ldb=%lld must be multiples of 8 (16-byte rows)",
+                             (long long)lda, (long long)ldb);
+        if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u)
+            return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: A and B must be 16-byte aligned");
+    }
+    const int64_t c_elem = c_f16 ? 2 : 4;
+    // C takes a TMA epilogue when a tensor map can describe it (16-byte
+    // aligned base and row pitch); an fp32 C accumulated into also has a
+    // scalar path, the written forms do not.
+    const bool c_tma = (reinterpret_cast<uintptr_t>(c) & 15u) == 0 && (ldc * c_elem) % 16 == 0;
+    if (!c_tma && overwrite)
         return set_error(CUDAIR_ERR_INVALID,
-                         "cudair: gemm: leading dimensions lda=%lld ldb=%lld ldc=%lld too small",
-                         (long long)lda, (long long)ldb, (long long)ldc);
-    if (lda % 8 || ldb % 8)
-        return set_error(CUDAIR_ERR_INVALID,
-                         "cudair: gemm: lda=%lld and ldb=%lld must be multiples of 8 (16-byte rows)",
-                         (long long)lda, (long long)ldb);
-    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u)
-        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: A and B must be 16-byte aligned");
+                         "cudair: gemm: a written C must be 16-byte aligned with a 16-byte row pitch");
     if (reinterpret_cast<uintptr_t>(c) & 3u)
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: C must be 4-byte aligned");
+    return CUDAIR_OK;
+}
+
+int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int64_t K, int64_t lda,
+                int64_t ldb, int64_t ldc, uint32_t flags, cudaStream_t stream) {
+    int rc = gemm_check(a, b, c, M, N, K, lda, ldb, ldc, flags);
+    if (rc != CUDAIR_OK) return rc;
+    const bool bf16 = flags & CUDAIR_GEMM_BF16, bt = flags & CUDAIR_GEMM_B_T;
+    const bool overwrite = flags & CUDAIR_GEMM_OVERWRITE, c_f16 = flags & CUDAIR_GEMM_C_F16;
+    if (M == 0 || N == 0 || (K == 0 && !overwrite)) return CUDAIR_OK;  // C = C
+    const int64_t c_elem = c_f16 ? 2 : 4;
+    const bool c_tma = (reinterpret_cast<uintptr_t>(c) & 15u) == 0 && (ldc * c_elem) % 16 == 0;
 
     DeviceInfo *dev = nullptr;
-    int rc = device_info(&dev);
+    rc = device_info(&dev);
     if (rc != CUDAIR_OK) return rc;
+    cudaError_t e;
+    if (K == 0) {  // C = 0: the product of an empty sum
+        e = cudaMemset2DAsync(c, static_cast<size_t>(ldc * c_elem), 0, static_cast<size_t>(N * c_elem),
+                              static_cast<size_t>(M), stream);
+        return e == cudaSuccess ? CUDAIR_OK : cuda_error(e, "cudaMemset2DAsync(C)");
+    }
 
     const int variant = g_variant.load();
-    // The few-row (stream-K) kernel takes M <= 64, and 64 < M <= 128 up to
+    // The few-row (stream-K) kernel takes the plain form (fp16, B as stored,
+    // fp32 C accumulated into) for M <= 64, and for 64 < M <= 128 up to
     // N = 8192.  Past that its re-reads of A from L2 (one per 128-column
     // tile) cost more than the single-CTA kernel's idle SMs (measured: at
     // M = 128, K = 8192: 51.0 against 54.6 us for N = 8192; at K = 4096,
     // 47.5 against 33.2 us for N = 14336).
-    const bool fewrows_auto = variant == 0 && (M <= 64 || (M <= 128 && N <= 8192));
+    if (variant == 3 && flags != 0)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm: the few-row kernel (variant 3) takes only the plain form (flags 0)");
+    const bool fewrows_auto = variant == 0 && flags == 0 && (M <= 64 || (M <= 128 && N <= 8192));
     if (variant == 3 || fewrows_auto)
-        return gemm_skinny_launch(a, b, c, static_cast<int>(M), static_cast<int>(N),
+        return gemm_skinny_launch(a, b, static_cast<float *>(c), static_cast<int>(M), static_cast<int>(N),
                                   static_cast<int>(K), lda, ldb, ldc, dev->sm_count, dev->status,
                                   stream);
     // 0 auto, 1 single CTA, 2 CTA pair (256 x 256), 4 CTA pair (256 x 512).
     const bool pair_auto = variant == 0 && M > 128 && dev->max_pairs > 0;
-    const int pair_nb = (variant == 4) ? 2
-                        : (variant == 2) ? 1
-                        : pair_auto ? gemm::auto_pair_nb(M, N, K, dev->max_pairs)
-                                    : 0;
-    const bool pair = pair_nb > 0;
-    alignas(64) CUtensorMap tmA, tmB;
+    const int nb = (variant == 4) ? 2
+                   : (variant == 2) ? 1
+                   : pair_auto ? gemm::auto_pair_nb(M, N, K, dev->max_pairs)
+                               : 0;
+    const uint32_t in_type = bf16 ? CUDAIR_TENSOR_MAP_BFLOAT16 : CUDAIR_TENSOR_MAP_FLOAT16;
+    alignas(64) CUtensorMap tmA, tmB, tmC = {};
     {
         const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
         const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
         const uint32_t box[2] = {64, 128};
-        rc = encode_tiled_internal(&tmA, CUDAIR_TENSOR_MAP_FLOAT16, 2,
-                                   reinterpret_cast<uint64_t>(a), dims, strides, box, nullptr,
-                                   CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B,
+        rc = encode_tiled_internal(&tmA, in_type, 2, reinterpret_cast<uint64_t>(a), dims, strides, box,
+                                   nullptr, CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B,
                                    CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
         if (rc != CUDAIR_OK) return rc;
     }
     {
-        const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
+        // B as stored: K rows of N (boxes of 64 n x 64 k); B^T: N rows of K
+        // (boxes of 64 k x 64 n).  Both boxes are 8 KB.
+        const uint64_t dims[2] = {static_cast<uint64_t>(bt ? K : N), static_cast<uint64_t>(bt ? N : K)};
         const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
-        const uint32_t box[2] = {64, gemm::BK};
-        rc = encode_tiled_internal(&tmB, CUDAIR_TENSOR_MAP_FLOAT16, 2,
-                                   reinterpret_cast<uint64_t>(b), dims, strides, box, nullptr,
-                                   CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B,
+        const uint32_t box[2] = {64, 64};
+        rc = encode_tiled_internal(&tmB, in_type, 2, reinterpret_cast<uint64_t>(b), dims, strides, box,
+                                   nullptr, CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B,
                                    CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
         if (rc != CUDAIR_OK) return rc;
     }
-
-    // C takes the TMA reduce-add epilogue when a tensor map can describe it
-    // (16-byte aligned base and row pitch); otherwise scalar loads and stores.
-    const int reduce = ((reinterpret_cast<uintptr_t>(c) & 15u) == 0 && ldc % 4 == 0) ? 1 : 0;
-    alignas(64) CUtensorMap tmC = {};
-    if (reduce) {
+    const int epi = c_f16 ? gemm::kEpiStoreF16
+                    : overwrite ? gemm::kEpiStoreF32
+                    : c_tma ? gemm::kEpiReduceF32
+                            : gemm::kEpiScalarAdd;
+    if (epi != gemm::kEpiScalarAdd) {
         const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
-        const uint64_t strides[1] = {static_cast<uint64_t>(ldc) * 4};
-        const uint32_t box[2] = {32, 32};
-        rc = encode_tiled_internal(&tmC, CUDAIR_TENSOR_MAP_FLOAT32, 2,
+        const uint64_t strides[1] = {static_cast<uint64_t>(ldc * c_elem)};
+        const uint32_t box[2] = {c_f16 ? 64u : 32u, 32u};  // 128-byte rows
+        rc = encode_tiled_internal(&tmC, c_f16 ? CUDAIR_TENSOR_MAP_FLOAT16 : CUDAIR_TENSOR_MAP_FLOAT32, 2,
                                    reinterpret_cast<uint64_t>(c), dims, strides, box, nullptr,
-                                   CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B,
-                                   CUDAIR_L2_PROMOTION_NONE, CUDAIR_OOB_FILL_NONE);
+                                   CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_NONE,
+                                   CUDAIR_OOB_FILL_NONE);
         if (rc != CUDAIR_OK) return rc;
     }
-    const int Mi = static_cast<int>(M), Ni = static_cast<int>(N), Ki = static_cast<int>(K);
-    const long long ldcl = static_cast<long long>(ldc);
-    cudaError_t e;
-    if (pair) {
-        const int tile_n = 256 * pair_nb;
-        const int64_t tiles = ((M + gemm::P_BM - 1) / gemm::P_BM) * ((N + tile_n - 1) / tile_n);
-        const int pairs = static_cast<int>(tiles < dev->max_pairs ? tiles : dev->max_pairs);
-        cudaLaunchConfig_t cfg = {};
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.gridDim = dim3(2 * pairs, 1, 1);
-        cfg.blockDim = dim3(gemm::THREADS, 1, 1);
-        cfg.stream = stream;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        if (pair_nb == 2) {
-            cfg.dynamicSmemBytes = gemm::PairCfg<2>::SMEM;
-            e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<2>, tmA, tmB, tmC, c, Mi, Ni, Ki, ldcl,
-                                   reduce);
-        } else {
-            cfg.dynamicSmemBytes = gemm::PairCfg<1>::SMEM;
-            e = cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_pair_kernel<1>, tmA, tmB, tmC, c, Mi, Ni, Ki, ldcl,
-                                   reduce);
-        }
-        if (e != cudaSuccess) return cuda_error(e, "gemm_f16f32_pair_kernel launch");
-    } else {
-        const int64_t tiles = ((M + gemm::S_BM - 1) / gemm::S_BM) * ((N + gemm::BN - 1) / gemm::BN);
-        const int grid = static_cast<int>(tiles < dev->sm_count ? tiles : dev->sm_count);
-        gemm::gemm_f16f32_kernel<<<grid, gemm::THREADS, gemm::S_SMEM, stream>>>(
-            tmA, tmB, tmC, c, Mi, Ni, Ki, ldcl, reduce);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return cuda_error(e, "gemm_f16f32_kernel launch");
-    }
+    float *cf = static_cast<float *>(c);
+    e = bt ? launch_square<true>(nb, *dev, tmA, tmB, tmC, cf, M, N, K, static_cast<long long>(ldc), bf16, epi,
+                                 stream)
+           : launch_square<false>(nb, *dev, tmA, tmB, tmC, cf, M, N, K, static_cast<long long>(ldc), bf16,
+                                  epi, stream);
+    if (e != cudaSuccess) return cuda_error(e, nb ? "gemm_f16f32_pair_kernel launch" : "gemm_f16f32_kernel launch");
     return CUDAIR_OK;
+}
+
+int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K,
+                       int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t stream) {
+    return gemm_launch(a, b, c, M, N, K, lda, ldb, ldc, 0u, stream);
 }
 
 }  // namespace cudair
@@ -860,6 +971,30 @@ CUDAIR_API int cudair_gemm_f16f32(const void *a, const void *b, float *c, int64_
                                   int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void *stream) {
     clear_error();
     return gemm_f16f32_launch(a, b, c, M, N, K, lda, ldb, ldc, static_cast<cudaStream_t>(stream));
+}
+
+CUDAIR_API int cudair_gemm(const void *a, const void *b, void *c, const float *bias, int64_t M,
+                           int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int64_t ldbias,
+                           uint32_t flags, void *stream) {
+    clear_error();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (bias) {
+        // C = A.B + bias: bias is copied into C, and the product added to it.
+        if (!(flags & CUDAIR_GEMM_OVERWRITE) || (flags & CUDAIR_GEMM_C_F16))
+            return set_error(CUDAIR_ERR_INVALID,
+                             "cudair: gemm: a bias needs CUDAIR_GEMM_OVERWRITE and an fp32 C");
+        int rc = gemm_check(a, b, c, M, N, K, lda, ldb, ldc, flags);
+        if (rc != CUDAIR_OK) return rc;
+        if (M == 0 || N == 0) return CUDAIR_OK;
+        if (ldbias < N)
+            return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: ldbias=%lld must be >= N", (long long)ldbias);
+        cudaError_t e = cudaMemcpy2DAsync(c, static_cast<size_t>(ldc) * 4, bias, static_cast<size_t>(ldbias) * 4,
+                                          static_cast<size_t>(N) * 4, static_cast<size_t>(M),
+                                          cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return cuda_error(e, "cudaMemcpy2DAsync(bias -> C)");
+        return gemm_launch(a, b, c, M, N, K, lda, ldb, ldc, flags & ~CUDAIR_GEMM_OVERWRITE, s);
+    }
+    return gemm_launch(a, b, c, M, N, K, lda, ldb, ldc, flags, s);
 }
 
 CUDAIR_API int cudair_set_gemm_variant(int variant) {

@@ -128,6 +128,16 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, uint32
         "r"(smem_src), "r"(x), "r"(y), "l"(cache_hint)
         : "memory");
 }
+// 2D tile store shared -> global (elements outside the tensor are skipped);
+// the same coordinate rules as the reduce above.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t smem_src, int32_t x,
+                                             int32_t y, uint64_t cache_hint) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint"
+        " [%0, {%2, %3}], [%1], %4;" ::"l"(reinterpret_cast<uint64_t>(map)),
+        "r"(smem_src), "r"(x), "r"(y), "l"(cache_hint)
+        : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -234,13 +244,15 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
         : "memory");
 }
 
-// Instruction descriptor for kind::f16 with fp16 A/B and fp32 D.
-//   bits 4-5 D format (1 = f32), 7-9 A format (0 = f16), 10-12 B format,
-//   15 A major (0 = K), 16 B major (1 = MN), 17-22 N/8, 24-28 M/16.
+// Instruction descriptor for kind::f16 with fp16 (or, with bf16, bfloat16)
+// A and B and fp32 D.
+//   bits 4-5 D format (1 = f32), 7-9 A format (0 = f16, 1 = bf16), 10-12 B
+//   format, 15 A major (0 = K), 16 B major (1 = MN), 17-22 N/8, 24-28 M/16.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t M, uint32_t N, bool a_mn_major,
-                                                     bool b_mn_major) {
-    return (1u << 4) | (0u << 7) | (0u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
-           ((b_mn_major ? 1u : 0u) << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+                                                     bool b_mn_major, bool bf16 = false) {
+    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+           ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) | ((N >> 3) << 17) |
+           ((M >> 4) << 24);
 }
 
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand tile:

@@ -58,6 +58,40 @@ def gemm(a, b, c, stream=None) -> None:
                                    a.stride(0), b.stride(0), c.stride(0), _stream(stream)))
 
 
+GEMM_BF16, GEMM_B_T, GEMM_OVERWRITE, GEMM_C_F16 = 0x1, 0x2, 0x4, 0x8
+
+
+def gemm_ex(a, b, c, bias=None, b_trans=False, overwrite=False, stream=None) -> None:
+    """The tensor-package GEMM family on the tcgen05 kernels (cudair_gemm):
+    c (+)= a @ B with B = b, or b.T when b_trans (b is N x K).  a and b are
+    both fp16 or both bf16; c is fp32 (accumulated into, or written when
+    overwrite) or fp16 (written: needs overwrite); bias (fp32 M x N) gives
+    c = a @ B + bias."""
+    import torch
+    if a.dtype not in (torch.float16, torch.bfloat16) or b.dtype != a.dtype:
+        raise CudairError(1, "cudair: gemm_ex: a and b must be both float16 or both bfloat16")
+    for t, nm in ((a, "a"), (b, "b"), (c, "c")):
+        _need(t, t.dtype, nm)
+        if t.stride(1) != 1:
+            raise CudairError(1, f"cudair: gemm_ex: {nm} needs unit inner stride")
+    if c.dtype not in (torch.float32, torch.float16):
+        raise CudairError(1, "cudair: gemm_ex: c must be float32 or float16")
+    M, K = a.shape
+    N = b.shape[0] if b_trans else b.shape[1]
+    if (b.shape[1] if b_trans else b.shape[0]) != K or tuple(c.shape) != (M, N):
+        raise CudairError(1, f"cudair: gemm_ex: shapes {tuple(a.shape)} {tuple(b.shape)} {tuple(c.shape)}")
+    flags = (GEMM_BF16 if a.dtype == torch.bfloat16 else 0) | (GEMM_B_T if b_trans else 0) | \
+        (GEMM_OVERWRITE if overwrite else 0) | (GEMM_C_F16 if c.dtype == torch.float16 else 0)
+    bias_ptr, ldbias = None, 0
+    if bias is not None:
+        _need(bias, torch.float32, "bias")
+        if tuple(bias.shape) != (M, N) or bias.stride(1) != 1:
+            raise CudairError(1, "cudair: gemm_ex: bias must be M x N with unit inner stride")
+        bias_ptr, ldbias = bias.data_ptr(), bias.stride(0)
+    check(lib().cudair_gemm(a.data_ptr(), b.data_ptr(), c.data_ptr(), bias_ptr, M, N, K, a.stride(0),
+                            b.stride(0), c.stride(0), ldbias, flags, _stream(stream)))
+
+
 def gemm_host(a_h, b_h, c_h, a_d, b_d, c_d, rows_per_block=0, stream=None) -> None:
     """c_h += a_h @ b_h from host (CPU) tensors, through the caller's device
     buffers a_d, b_d, c_d (dense, same shapes): copies in, GEMM and copy out

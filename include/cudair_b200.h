@@ -155,6 +155,36 @@ int cudair_gemm_f16f32(const void *a, const void *b, float *c,
                        int64_t lda, int64_t ldb, int64_t ldc, void *stream);
 
 /*
+ * The GEMM family of the reference's examples/tensor package (tensor.go:15-98:
+ * MmaF16, MmaF16Bias, MmaF16Trans, MmaF16Half, MmaBF16, each an n x n matmul
+ * of one warp per 16 x 8 tile) on the tuned tcgen05 kernels, for any
+ * M x N x K:
+ *   flags 0                      C (fp32) += A . B, as cudair_gemm_f16f32
+ *   CUDAIR_GEMM_OVERWRITE        C = A . B                          (MmaF16)
+ *   ... with bias != NULL        C = A . B + bias (bias M x N fp32, pitch
+ *                                ldbias; copied into C, then added to)
+ *                                                              (MmaF16Bias)
+ *   CUDAIR_GEMM_B_T              b holds B^T: N x K row-major, pitch ldb >= K
+ *                                                             (MmaF16Trans)
+ *   CUDAIR_GEMM_C_F16 | OVERWRITE  C is fp16 (pitch ldc in halves): the
+ *                                fp32 product rounded once to half  (MmaF16Half)
+ *   CUDAIR_GEMM_BF16             A and B are bfloat16                (MmaBF16)
+ * Flags combine.  A written C (OVERWRITE) needs a 16-byte aligned base and a
+ * 16-byte row pitch.  MmaF16Half accumulates in half; here the sum is kept
+ * in fp32 and rounded once, which is identical whenever the half sums are
+ * exact (the reference's tests) and closer to the exact product otherwise.
+ * Other rules as cudair_gemm_f16f32.  Asynchronous on stream.
+ */
+#define CUDAIR_GEMM_BF16 0x1u
+#define CUDAIR_GEMM_B_T 0x2u
+#define CUDAIR_GEMM_OVERWRITE 0x4u
+#define CUDAIR_GEMM_C_F16 0x8u
+int cudair_gemm(const void *a, const void *b, void *c, const float *bias,
+                int64_t M, int64_t N, int64_t K,
+                int64_t lda, int64_t ldb, int64_t ldc, int64_t ldbias,
+                uint32_t flags, void *stream);
+
+/*
  * Selects the GEMM kernel variant for subsequent calls in this process:
  * 0 = automatic (few-row kernel when M <= 64, and when M <= 128 with
  * N <= 8192; single CTAs with 128 x 256 tiles for the rest of M <= 128; else CTA pairs with 256 x 256 or 256 x 512 tiles, whichever a

@@ -136,6 +136,21 @@ def test_gemm_pdl_mode_validation(cudair):
         assert L.cudair_set_gemm_pdl(mode) == 0
 
 
+@pytest.mark.parametrize("flags,bias,c,ldc,needle", [
+    (0x8, None, 16, 16, "needs CUDAIR_GEMM_OVERWRITE"),
+    (0x10, None, 16, 16, "unknown flags"),
+    (0x0, 16, 16, 16, "a bias needs"),
+    (0xC, 16, 16, 16, "a bias needs"),
+    (0x4, None, 20, 16, "16-byte aligned"),
+    (0x4, None, 16, 18, "16-byte aligned"),
+    (0x2, None, 16, 16, "leading dimensions"),
+])
+def test_gemm_family_validation(cudair, flags, bias, c, ldc, needle):
+    # M = N = 16, K = 32: with B^T (flag 0x2) ldb = 16 < K is too small.
+    rc = cudair.lib().cudair_gemm(16, 16, c, bias, 16, 16, 32, 32, 16, ldc, 16, flags, None)
+    assert rc == 1 and needle in cudair.last_error(), cudair.last_error()
+
+
 def test_vecadd_and_reduce_validation(cudair):
     L = cudair.lib()
     assert L.cudair_vecadd(None, None, None, -1, None) == 1
