@@ -15,12 +15,14 @@ is needed between steps.
 
 One step = one launch of the tcgen05 GEMM over the GPU's shard.  `value` is
 the aggregate TFLOP/s over all ranks (2 M N K per step / the max over ranks of
-the device-timed step).  `e2e` times the same step through the C ABI with
-host buffers: pinned host -> device copies of A, B, C, the launch, and the
-device -> host copy of C, all inside the timed region.  The line also
-carries VecAdd (n = 2^28 fp32 per GPU, HBM-bound) and the decode-shaped GEMM
-(M=16, N=14336, K=4096, three copies of B cycled so each step reads B from
-HBM) as secondary results, each against its roofline.
+the device-timed step).  `e2e` times the same step through the C ABI's host
+entry (cudair_gemm_f16f32_host): pinned host -> device copies of A, B, C, the
+GEMM, and the device -> host copy of C, all inside the timed region, the
+copies of one block of rows overlapping the GEMM of another.  The line also
+carries VecAdd, Saxpy and Square (n = 2^28 fp32 per GPU, HBM-bound) and the
+decode-shaped GEMM (M=16, N=14336, K=4096, three copies of B cycled so each
+launch reads B from HBM, timed from a CUDA graph) as secondary results, each
+against its roofline.
 
 `--impl reference` times the reference's CPU implementation of the path (the
 i-j-k float32 loop of its tests, restated in C under oracle/) on all host
@@ -370,6 +372,20 @@ def run_vecadd(args, world, rank, dev, g, kernels):
     return ms, 3 * 4 * VEC_N / (ms * 1e-3) / 1e9
 
 
+def run_saxpy_square(args, world, rank, dev, g, kernels):
+    """Saxpy (12 bytes per element: read x and y, write y) and Square (8: read
+    and write x) over n = 2^28 fp32 per GPU, each step one launch."""
+    import torch
+    g.manual_seed(4100 + rank)
+    x = torch.rand(VEC_N, generator=g, device=dev) * 2 - 1
+    y = torch.rand(VEC_N, generator=g, device=dev) * 2 - 1
+    ms_saxpy = time_steps(lambda: kernels.saxpy(0.5, x, y), args.steps, args.warmup, world, dev)
+    ms_square = time_steps(lambda: kernels.square(x), args.steps, args.warmup, world, dev)
+    del x, y
+    return {"saxpy": (ms_saxpy, 12 * VEC_N / (ms_saxpy * 1e-3) / 1e9),
+            "square": (ms_square, 8 * VEC_N / (ms_square * 1e-3) / 1e9)}
+
+
 def run_skinny(args, world, rank, dev, g, kernels):
     """M=16, N=14336, K=4096 (decode-shaped): B is 117 MB, so three copies of
     it are cycled (351 MB > L2) and every launch streams its B from HBM.  A
@@ -459,6 +475,7 @@ def run_ours(args, world, rank, local):
     torch.cuda.empty_cache()
     gather = run_gather(world, dev, M, N) if (args.gather and world > 1) else None
     v_ms, v_gbs = run_vecadd(args, world, rank, dev, g, kernels)
+    streams = run_saxpy_square(args, world, rank, dev, g, kernels)
     sm, sn, sk = SKINNY
     s_ms, s_gbs = run_skinny(args, world, rank, dev, g, kernels)
     kernels.wait_status(clear=True)
@@ -497,6 +514,10 @@ def run_ours(args, world, rank, local):
                                 "unit": "GB/s", "frac": v_gbs / peaks["hbm_gbs"],
                                 "traffic": traffic.get("vecadd_2p28"),
                                 "frac_of_nominal": v_gbs / 8000.0}},
+        **{name: {"value": gbs * world, "unit": "GB/s", "ms_per_step": ms, "n_per_gpu": VEC_N,
+                  "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                               "frac": gbs / peaks["hbm_gbs"]}}
+           for name, (ms, gbs) in streams.items()},
         "skinny": {"M": sm, "N": sn, "K": sk, "ms": s_ms, "GB/s": s_gbs,
                    "timing": "CUDA graph of 30 launches cycling 3 copies of B, per launch; "
                              "programmatic dependent launch, B requested before the wait",

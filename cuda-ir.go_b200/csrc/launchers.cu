@@ -9,26 +9,68 @@
 
 using namespace cudair;
 
-// VecAdd on a persistent grid: 4 CTAs of 512 threads per SM (every SM kept
-// at full occupancy, 16 loads of 16 bytes in flight per thread pair), capped
-// by the work so small n does not launch idle CTAs.
+namespace {
+
+constexpr int kStreamThreads = 512;
+
+// The persistent grid of the streaming kernels (VecAdd, Saxpy, Square): 4
+// CTAs of 512 threads per SM (every SM kept at full occupancy, 16 loads of 16
+// bytes in flight per thread pair), capped by the work so small n does not
+// launch idle CTAs.
+int stream_grid(int32_t n, unsigned *blocks_out) {
+    int sms = 0;
+    int rc = sm_count_current_device(&sms);
+    if (rc != CUDAIR_OK) return rc;
+    const int64_t vec_work = (static_cast<int64_t>(n) + 3) / 4;
+    int64_t blocks = (vec_work + kStreamThreads - 1) / kStreamThreads;
+    const int64_t cap = static_cast<int64_t>(sms) * 4;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    *blocks_out = static_cast<unsigned>(blocks);
+    return CUDAIR_OK;
+}
+
+}  // namespace
+
 CUDAIR_API int cudair_vecadd(const float *a, const float *b, float *out, int32_t n, void *stream) {
     clear_error();
     if (n < 0) return set_error(CUDAIR_ERR_INVALID, "cudair: VecAdd: n = %d", n);
     if (n == 0) return CUDAIR_OK;
     if (!a || !b || !out) return set_error(CUDAIR_ERR_INVALID, "cudair: VecAdd: nil pointer");
-    int sms = 0;
-    int rc = sm_count_current_device(&sms);
+    unsigned blocks = 0;
+    int rc = stream_grid(n, &blocks);
     if (rc != CUDAIR_OK) return rc;
-    constexpr int kThreads = 512;
-    const int64_t vec_work = (static_cast<int64_t>(n) + 3) / 4;
-    int64_t blocks = (vec_work + kThreads - 1) / kThreads;
-    const int64_t cap = static_cast<int64_t>(sms) * 4;
-    if (blocks > cap) blocks = cap;
-    if (blocks < 1) blocks = 1;
-    VecAdd<<<static_cast<unsigned>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, b, out, n);
+    VecAdd<<<blocks, kStreamThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, b, out, n);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "VecAdd launch");
+    return CUDAIR_OK;
+}
+
+CUDAIR_API int cudair_saxpy(float alpha, const float *x, float *y, int32_t n, void *stream) {
+    clear_error();
+    if (n < 0) return set_error(CUDAIR_ERR_INVALID, "cudair: Saxpy: n = %d", n);
+    if (n == 0) return CUDAIR_OK;
+    if (!x || !y) return set_error(CUDAIR_ERR_INVALID, "cudair: Saxpy: nil pointer");
+    unsigned blocks = 0;
+    int rc = stream_grid(n, &blocks);
+    if (rc != CUDAIR_OK) return rc;
+    Saxpy<<<blocks, kStreamThreads, 0, static_cast<cudaStream_t>(stream)>>>(alpha, x, y, n);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "Saxpy launch");
+    return CUDAIR_OK;
+}
+
+CUDAIR_API int cudair_square(float *x, int32_t n, void *stream) {
+    clear_error();
+    if (n < 0) return set_error(CUDAIR_ERR_INVALID, "cudair: Square: n = %d", n);
+    if (n == 0) return CUDAIR_OK;
+    if (!x) return set_error(CUDAIR_ERR_INVALID, "cudair: Square: nil pointer");
+    unsigned blocks = 0;
+    int rc = stream_grid(n, &blocks);
+    if (rc != CUDAIR_OK) return rc;
+    Square<<<blocks, kStreamThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, n);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "Square launch");
     return CUDAIR_OK;
 }
 

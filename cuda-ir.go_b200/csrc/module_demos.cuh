@@ -56,25 +56,6 @@ __device__ __forceinline__ bool mbar_wait_parity(uint64_t *bar, uint32_t parity)
 
 }  // namespace cudair_demo
 
-// ---- vecadd package: Saxpy, Square (examples/vecadd/vecadd.go:13-28) --------
-
-// y = alpha * x + y with a grid-stride loop (vecadd.go:13-18).  The product
-// and the sum are rounded separately (no fused multiply-add), as the
-// reference's CPU check computes them.
-extern "C" __global__ void Saxpy(float alpha, const float *__restrict__ x, float *__restrict__ y,
-                                 int n) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
-        y[i] = __fadd_rn(__fmul_rn(alpha, x[i]), y[i]);
-}
-
-// x[i] = x[i] * x[i] in place (vecadd.go:20-28).
-extern "C" __global__ void Square(float *__restrict__ x, int n) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
-        x[i] = __fmul_rn(x[i], x[i]);
-}
-
 // ---- hopper package (examples/hopper/hopper.go) ------------------------------
 
 // Clusters of two blocks: each block fills its shared tile with

@@ -75,6 +75,103 @@ extern "C" __global__ void __launch_bounds__(1024)
     }
 }
 
+// ---- Saxpy, Square (the rest of the vecadd package) ------------------------------
+
+// y[i] = alpha * x[i] + y[i] for i < n (examples/vecadd/vecadd.go:13-18),
+// streamed like VecAdd: 16-byte vectors, four per trip with every load issued
+// first, streaming cache policy, scalar head and tail, and a scalar loop when
+// x and y do not share their offset within 16 bytes.  The product and the sum
+// are rounded separately (no fused multiply-add), as the reference's CPU check
+// computes them (vecadd/run/main.go:62-69).
+extern "C" __global__ void __launch_bounds__(1024)
+    Saxpy(float alpha, const float *__restrict__ x, float *__restrict__ y, int n) {
+    if (n <= 0) return;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const uintptr_t mis = reinterpret_cast<uintptr_t>(y) & 15u;
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) == mis && (mis & 3u) == 0) {
+        int64_t head = static_cast<int64_t>((16u - mis) & 15u) >> 2;
+        if (head > n) head = n;
+        if (tid < head) y[tid] = __fadd_rn(__fmul_rn(alpha, x[tid]), y[tid]);
+        const int64_t n4 = (n - head) >> 2;
+        const float4 *x4 = reinterpret_cast<const float4 *>(x + head);
+        float4 *y4 = reinterpret_cast<float4 *>(y + head);
+        constexpr int U = 4;
+        int64_t i = tid;
+        for (; i + (U - 1) * nthr < n4; i += U * nthr) {
+            float4 vx[U], vy[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                vx[u] = __ldcs(x4 + i + u * nthr);
+                vy[u] = __ldcs(y4 + i + u * nthr);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float4 r;
+                r.x = __fadd_rn(__fmul_rn(alpha, vx[u].x), vy[u].x);
+                r.y = __fadd_rn(__fmul_rn(alpha, vx[u].y), vy[u].y);
+                r.z = __fadd_rn(__fmul_rn(alpha, vx[u].z), vy[u].z);
+                r.w = __fadd_rn(__fmul_rn(alpha, vx[u].w), vy[u].w);
+                __stcs(y4 + i + u * nthr, r);
+            }
+        }
+        for (; i < n4; i += nthr) {
+            const float4 vx = __ldcs(x4 + i), vy = __ldcs(y4 + i);
+            float4 r;
+            r.x = __fadd_rn(__fmul_rn(alpha, vx.x), vy.x);
+            r.y = __fadd_rn(__fmul_rn(alpha, vx.y), vy.y);
+            r.z = __fadd_rn(__fmul_rn(alpha, vx.z), vy.z);
+            r.w = __fadd_rn(__fmul_rn(alpha, vx.w), vy.w);
+            __stcs(y4 + i, r);
+        }
+        const int64_t t = head + 4 * n4 + tid;
+        if (t < n) y[t] = __fadd_rn(__fmul_rn(alpha, x[t]), y[t]);
+    } else {
+        for (int64_t i = tid; i < n; i += nthr) y[i] = __fadd_rn(__fmul_rn(alpha, x[i]), y[i]);
+    }
+}
+
+// x[i] = x[i] * x[i] in place (vecadd.go:20-28; the reference gives each
+// thread one element), streamed like VecAdd.
+extern "C" __global__ void __launch_bounds__(1024) Square(float *__restrict__ x, int n) {
+    if (n <= 0) return;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const uintptr_t mis = reinterpret_cast<uintptr_t>(x) & 15u;
+    if ((mis & 3u) == 0) {
+        int64_t head = static_cast<int64_t>((16u - mis) & 15u) >> 2;
+        if (head > n) head = n;
+        if (tid < head) x[tid] = __fmul_rn(x[tid], x[tid]);
+        const int64_t n4 = (n - head) >> 2;
+        float4 *x4 = reinterpret_cast<float4 *>(x + head);
+        constexpr int U = 4;
+        int64_t i = tid;
+        for (; i + (U - 1) * nthr < n4; i += U * nthr) {
+            float4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) v[u] = __ldcs(x4 + i + u * nthr);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float4 r;
+                r.x = __fmul_rn(v[u].x, v[u].x);
+                r.y = __fmul_rn(v[u].y, v[u].y);
+                r.z = __fmul_rn(v[u].z, v[u].z);
+                r.w = __fmul_rn(v[u].w, v[u].w);
+                __stcs(x4 + i + u * nthr, r);
+            }
+        }
+        for (; i < n4; i += nthr) {
+            const float4 v = __ldcs(x4 + i);
+            __stcs(x4 + i, make_float4(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y), __fmul_rn(v.z, v.z),
+                                       __fmul_rn(v.w, v.w)));
+        }
+        const int64_t t = head + 4 * n4 + tid;
+        if (t < n) x[t] = __fmul_rn(x[t], x[t]);
+    } else {
+        for (int64_t i = tid; i < n; i += nthr) x[i] = __fmul_rn(x[i], x[i]);
+    }
+}
+
 // ---- MatMul16 ---------------------------------------------------------------
 
 namespace cudair_detail {

@@ -45,6 +45,8 @@ SIGNATURES = {
     "cudair_set_gemm_variant": (c_int, [c_int]),
     "cudair_set_gemm_pdl": (c_int, [c_int]),
     "cudair_vecadd": (c_int, [c_vp, c_vp, c_vp, ctypes.c_int32, c_vp]),
+    "cudair_saxpy": (c_int, [ctypes.c_float, c_vp, c_vp, ctypes.c_int32, c_vp]),
+    "cudair_square": (c_int, [c_vp, ctypes.c_int32, c_vp]),
     "cudair_reduce_f32": (c_int, [c_vp, c_vp, ctypes.c_int32, c_vp]),
     "cudair_wait_status": (c_int, [_u32p, c_int]),
     "cudair_wait_timeout_selftest": (c_int, [c_u64, c_vp]),

@@ -142,6 +142,23 @@ def vecadd(a, b, out, stream=None) -> None:
     check(lib().cudair_vecadd(a.data_ptr(), b.data_ptr(), out.data_ptr(), n, _stream(stream)))
 
 
+def saxpy(alpha, x, y, stream=None) -> None:
+    """y = alpha * x + y over fp32 vectors (Saxpy's operands)."""
+    import torch
+    _need(x, torch.float32, "x")
+    _need(y, torch.float32, "y")
+    if x.numel() != y.numel():
+        raise CudairError(1, "cudair: Saxpy: length mismatch")
+    check(lib().cudair_saxpy(float(alpha), x.data_ptr(), y.data_ptr(), y.numel(), _stream(stream)))
+
+
+def square(x, stream=None) -> None:
+    """x = x * x in place over an fp32 vector (Square's operand)."""
+    import torch
+    _need(x, torch.float32, "x")
+    check(lib().cudair_square(x.data_ptr(), x.numel(), _stream(stream)))
+
+
 def reduce_f32(x, out, stream=None) -> None:
     """out[2w], out[2w+1] = min, max of warp w's 32 values (ReduceF32)."""
     import torch

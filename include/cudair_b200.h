@@ -262,6 +262,15 @@ int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c,
 int cudair_vecadd(const float *a, const float *b, float *out, int32_t n, void *stream);
 
 /*
+ * The rest of the vecadd package (vecadd.go:13-28), streamed like VecAdd on
+ * a persistent grid: y[i] = alpha * x[i] + y[i] (product and sum rounded
+ * separately, as the reference's check computes them) and x[i] = x[i] * x[i]
+ * in place.  Any alignment.  Asynchronous.
+ */
+int cudair_saxpy(float alpha, const float *x, float *y, int32_t n, void *stream);
+int cudair_square(float *x, int32_t n, void *stream);
+
+/*
  * Per-warp min and max of n floats: out[2w], out[2w+1] for warp w
  * (blackwell.go:8-17, redux.sync.{min,max}.f32).  n must be a multiple of 32.
  */
