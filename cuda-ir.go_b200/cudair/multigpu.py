@@ -54,39 +54,60 @@ def max_over_ranks(x: float, world: int, device=None) -> float:
     return float(t.item())
 
 
+def any_rank(flag: bool, world: int, device=None) -> bool:
+    """True on every rank when flag is true on any rank (one all-reduce: the
+    same collective step everywhere, so a local failure cannot leave the
+    other ranks waiting in a later collective)."""
+    return max_over_ranks(1.0 if flag else 0.0, world, device) > 0.0
+
+
 def replicate_from_rank0(buf, rank: int, world: int,
                          copy_fn: Optional[Callable[[int, int, int], float]] = None) -> float:
     """Makes every rank's `buf` (a CUDA tensor of the same size on each GPU)
     equal to rank 0's by one peer copy over NVLink; returns the copy time in
     ms on this rank (0 on rank 0).
 
-    copy_fn(dst_ptr, handle_bytes..., nbytes) may replace the GPU copy (tests);
-    by default the C ABI does it: cudair_ipc_export on rank 0,
-    cudair_ipc_open / cudair_peer_copy / cudair_ipc_close on the others."""
+    copy_fn(kind, buf, arg) may replace the GPU copy (tests); by default the C
+    ABI does it: cudair_ipc_export on rank 0, cudair_ipc_open /
+    cudair_peer_copy / cudair_ipc_close on the others.
+
+    Failures are collective: if rank 0 cannot export, it sends the error in
+    place of the handle, and if any rank cannot copy, an all-reduce tells
+    every rank; all ranks then raise RuntimeError after the same collective
+    steps, so none is left waiting for a peer that gave up."""
     if world == 1:
         return 0.0
-    import torch.distributed as dist
     from . import _lib
     nbytes = buf.numel() * buf.element_size()
-    handle = None
+    payload = None
     if rank == 0:
-        if copy_fn is None:
-            h = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
-            off = ctypes.c_uint64()
-            _lib.check(_lib.lib().cudair_ipc_export(ctypes.c_void_p(buf.data_ptr()), h,
-                                                    ctypes.byref(off)))
-            # The handle maps the whole allocation; the offset locates buf in it.
-            handle = bytes(h) + off.value.to_bytes(8, "little")
-        else:
-            handle = copy_fn("export", buf, nbytes)
-    handle = exchange_from_rank0(handle, rank, world)
-    ms = 0.0
+        try:
+            if copy_fn is None:
+                h = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
+                off = ctypes.c_uint64()
+                _lib.check(_lib.lib().cudair_ipc_export(ctypes.c_void_p(buf.data_ptr()), h,
+                                                        ctypes.byref(off)))
+                # The handle maps the whole allocation; the offset locates buf in it.
+                handle = bytes(h) + off.value.to_bytes(8, "little")
+            else:
+                handle = copy_fn("export", buf, nbytes)
+            payload = b"OK" + handle
+        except Exception as e:  # reported to every rank below
+            payload = b"ER" + f"{type(e).__name__}: {e}".encode()
+    payload = exchange_from_rank0(payload, rank, world)
+    if payload[:2] != b"OK":
+        raise RuntimeError("replicate_from_rank0: rank 0 could not export B: " + payload[2:].decode())
+    handle = payload[2:]
+    ms, err = 0.0, None
     if rank != 0:
-        if copy_fn is None:
-            ms = _peer_copy_cuda(buf, handle, nbytes)
-        else:
-            ms = copy_fn("import", buf, handle)
-    dist.barrier()  # rank 0 keeps B alive until every copy has landed
+        try:
+            ms = _peer_copy_cuda(buf, handle, nbytes) if copy_fn is None else copy_fn("import", buf, handle)
+        except Exception as e:
+            err = f"{type(e).__name__}: {e}"
+    # Also the barrier that keeps rank 0's B alive until every copy has landed.
+    if any_rank(err is not None, world, buf.device if buf.is_cuda else None):
+        raise RuntimeError("replicate_from_rank0: a peer copy failed"
+                           + (f" on this rank ({err})" if err else " on another rank"))
     return ms
 
 
