@@ -418,6 +418,11 @@ int workspace(Workspace **out) {
         if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(skinny workspace)");
         e = cudaMemset(w.ptr, 0, kWorkspaceBytes);
         if (e != cudaSuccess) return cuda_error(e, "cudaMemset(skinny workspace)");
+        // The zeroing runs on the legacy default stream; a launch on a
+        // non-blocking stream is not ordered after it, so wait for it here
+        // (once per device).
+        e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_error(e, "cudaDeviceSynchronize(skinny workspace)");
         w.bytes = kWorkspaceBytes;
     }
     if (!w.attr_set) {
@@ -463,6 +468,7 @@ int skinny_reset_workspace() {
     std::lock_guard<std::mutex> lk(g_ws_mu);
     if (g_ws[dev].ptr) {
         cudaError_t e = cudaMemset(g_ws[dev].ptr, 0, g_ws[dev].bytes);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e != cudaSuccess) return cuda_error(e, "cudaMemset(skinny workspace)");
     }
     return CUDAIR_OK;

@@ -187,16 +187,19 @@ int cudair_gemm(const void *a, const void *b, void *c, const float *bias,
 /*
  * Selects the GEMM kernel variant for subsequent calls in this process:
  * 0 = automatic (few-row kernel when M <= 64, and when M <= 128 with
- * N <= 8192; single CTAs with 128 x 256 tiles for the rest of M <= 128; else CTA pairs with 256 x 256 or 256 x 512 tiles, whichever a
- * makespan estimate for the shape favours), 1 = single CTA, 2 = CTA pair
+ * N <= 8192; single CTAs with 128 x 256 tiles for the rest of M <= 128;
+ * else CTA pairs with 256 x 256 or 256 x 512 tiles, whichever a makespan
+ * estimate for the shape favours), 1 = single CTA, 2 = CTA pair
  * with 256 x 256 tiles, 3 = few-row kernel (M <= 128 only), 4 = CTA pair
  * with 256 x 512 tiles.  All variants compute the same result within fp32
  * rounding; the choice only affects speed.
  *
  * The few-row kernel (B as the MMA's 128-row side, K split evenly over all
- * SMs) keeps its partial sums in a 21.25 MB per-device workspace that the
- * library allocates on its first use on a device; its calls on one device
- * must not overlap in time (issue them on one stream).
+ * SMs) keeps its partial sums and tile counters in a 21.25 MB per-device
+ * workspace that the library allocates, zeroes and synchronises on its first
+ * use on a device (make that call before any stream capture).  Its calls on
+ * one device must not overlap in time: issue them on one stream, or order the
+ * streams with events, as with a single cuBLAS workspace.
  */
 int cudair_set_gemm_variant(int variant);
 
