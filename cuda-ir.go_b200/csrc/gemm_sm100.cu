@@ -100,7 +100,10 @@ struct PairCfg {
 
 static_assert(S_SMEM <= 227 * 1024, "shared memory budget");
 
-// Row-block / column-block of persistent tile index t (grouped raster).
+// Row-block / column-block of persistent tile index t: groups of group_m
+// row-blocks, visited column by column, with the column order reversed in
+// every other group (so a group starts on the B column-panels the previous
+// one ended on, still in L2: ~0.6 % faster than one direction at 8192^3).
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int &m_blk,
                                             int &n_blk) {
     const int per_group = group_m * num_n;
@@ -110,6 +113,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int gro
     const int r = t - group * per_group;
     m_blk = first_m + r % gsize;
     n_blk = r / gsize;
+    if (group & 1) n_blk = num_n - 1 - n_blk;
 }
 
 // Bounded wait that ignores the abort flag: used while unwinding.

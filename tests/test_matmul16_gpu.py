@@ -301,3 +301,58 @@ def test_gemm_c_layouts(dev, cudair, variant, c_offset, ldc_pad):
     assert np.array_equal(body[:, :N], want)
     assert np.all(body[:, N:] == -7.0)
     assert np.all(got[:c_offset] == -7.0) and np.all(got[c_offset + M * ldc:] == -7.0)
+
+
+@pytest.mark.parametrize("variant_id", [0, 4], ids=["auto", "pairwide"])
+def test_gemm_c_beyond_2p31_elements(dev, cudair, variant_id):
+    # C with more than 2^31 elements (65600 x 32776 fp32 = 8.6 GB): no 32-bit
+    # index overflows in the tiles, the tensor-map coordinates or the
+    # epilogue.  Integer operands (exact); rows around the 2^31-element
+    # boundary, the ragged last tile and the last row are checked against
+    # int64 products.
+    import torch
+    from cudair import kernels
+    M, N, K = 65600, 32776, 64
+    i = torch.arange(M, device=dev, dtype=torch.int32).view(M, 1)
+    k = torch.arange(K, device=dev, dtype=torch.int32).view(1, K)
+    a = ((i + 2 * k) % 7 - 3).half()
+    kk = torch.arange(K, device=dev, dtype=torch.int32).view(K, 1)
+    j = torch.arange(N, device=dev, dtype=torch.int32).view(1, N)
+    b = ((3 * kk + j) % 5 - 2).half()
+    c = (j - i).float()  # c[i][j] = j - i, as the reference's generator
+    kernels.set_gemm_variant(variant_id)
+    try:
+        kernels.gemm(a, b, c)
+        torch.cuda.synchronize()
+    finally:
+        kernels.set_gemm_variant(0)
+    boundary = (1 << 31) // N
+    rows = sorted({0, 1, boundary - 1, boundary, boundary + 1, M - 65, M - 64, M - 2, M - 1})
+    bf = b.cpu().numpy().astype(np.int64)
+    for r in rows:
+        ar = a[r].cpu().numpy().astype(np.int64)
+        want = ar @ bf + (np.arange(N, dtype=np.int64) - r)
+        got = c[r].cpu().numpy()
+        assert np.array_equal(got, want.astype(np.float32)), r
+    del a, b, c
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("M", [1, 16])
+@pytest.mark.parametrize("kb", [2, 3, 4, 5, 6, 8, 16])
+def test_fewrows_contributors_per_tile(dev, cudair, M, kb):
+    # With fewer 64-wide k-blocks than SMs, every k-block has its own CTA, so
+    # each 128-column tile has exactly kb contributors; their parts must all
+    # be summed, whichever contributor finishes last.  Exact (integer data),
+    # twice in a row from the same C (bit-identical, timing-independent).
+    import torch
+    from cudair import kernels
+    for N in (128, 264):
+        K = 64 * kb
+        af, bf, c, want = kat(M, N, K)
+        da, db = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16)
+        for _ in range(2):
+            dc = _dev(c, dev, torch.float32)
+            kernels.gemm(da, db, dc)
+            got = dc.cpu().numpy()
+            assert np.array_equal(got, want), (N, K)
