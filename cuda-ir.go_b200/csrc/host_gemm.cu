@@ -87,7 +87,9 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_host: negative size M=%lld N=%lld K=%lld",
                          (long long)M, (long long)N, (long long)K);
     if (M == 0 || N == 0) return CUDAIR_OK;  // C has no elements
-    if (!a_host || !b_host || !c_host || !a_dev || !b_dev || !c_dev)
+    // b_host may be NULL: B is then already in b_dev (replicated on the
+    // device, e.g. over NVLink), and only A and C cross the host link.
+    if (!a_host || !c_host || !a_dev || !b_dev || !c_dev)
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_host: nil pointer");
     if (lda < K || ldb < N || ldc < N)
         return set_error(CUDAIR_ERR_INVALID,
@@ -129,7 +131,7 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
     CUDAIR_TRY(cudaStreamWaitEvent(p->out, p->start, 0), "cudaStreamWaitEvent");
     const size_t a_row = static_cast<size_t>(K) * 2, b_row = static_cast<size_t>(N) * 2,
                  c_row = static_cast<size_t>(N) * 4;
-    if (K > 0) {
+    if (K > 0 && b_host) {
         CUDAIR_TRY(copy_rows(b_dev, b_row, b_host, static_cast<size_t>(ldb) * 2, b_row,
                              static_cast<size_t>(K), cudaMemcpyHostToDevice, p->in),
                    "H2D of B");

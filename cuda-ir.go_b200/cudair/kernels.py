@@ -95,12 +95,14 @@ def gemm_ex(a, b, c, bias=None, b_trans=False, overwrite=False, stream=None) -> 
 def gemm_host(a_h, b_h, c_h, a_d, b_d, c_d, rows_per_block=0, stream=None) -> None:
     """c_h += a_h @ b_h from host (CPU) tensors, through the caller's device
     buffers a_d, b_d, c_d (dense, same shapes): copies in, GEMM and copy out
-    pipelined over row blocks.  Asynchronous on `stream`; c_h holds the result
+    pipelined over row blocks.  b_h = None: b_d already holds B.  Asynchronous on `stream`; c_h holds the result
     once the stream is synchronised.  Pinned host tensors let the copies
     overlap."""
     import torch
     for t, dt, nm in ((a_h, torch.float16, "a_h"), (b_h, torch.float16, "b_h"),
                       (c_h, torch.float32, "c_h")):
+        if t is None and nm == "b_h":
+            continue  # B already in b_d
         if not isinstance(t, torch.Tensor) or t.is_cuda or t.dtype != dt or t.stride(1) != 1:
             raise CudairError(1, f"cudair: gemm_host: {nm} must be a host {dt} tensor, unit inner stride")
     for t, dt, nm in ((a_d, torch.float16, "a_d"), (b_d, torch.float16, "b_d"),
@@ -109,12 +111,13 @@ def gemm_host(a_h, b_h, c_h, a_d, b_d, c_d, rows_per_block=0, stream=None) -> No
         if not t.is_contiguous():
             raise CudairError(1, f"cudair: gemm_host: {nm} must be contiguous")
     M, K = a_h.shape
-    K2, N = b_h.shape
+    K2, N = b_d.shape
     if K2 != K or tuple(c_h.shape) != (M, N) or tuple(a_d.shape) != (M, K) or \
-            tuple(b_d.shape) != (K, N) or tuple(c_d.shape) != (M, N):
+            tuple(c_d.shape) != (M, N) or (b_h is not None and tuple(b_h.shape) != (K, N)):
         raise CudairError(1, "cudair: gemm_host: shapes do not match")
     check(lib().cudair_gemm_f16f32_host(
-        a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, N, K, a_h.stride(0), b_h.stride(0),
+        a_h.data_ptr(), None if b_h is None else b_h.data_ptr(), c_h.data_ptr(), M, N, K,
+        a_h.stride(0), N if b_h is None else b_h.stride(0),
         c_h.stride(0), a_d.data_ptr(), b_d.data_ptr(), c_d.data_ptr(), rows_per_block,
         _stream(stream)))
 

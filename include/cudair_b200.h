@@ -223,7 +223,9 @@ int cudair_set_gemm_pdl(int mode);
  * gocudrv CopyFrom, launches MatMul16 and copies C back with CopyTo) as one
  * call.  a_host (M x K fp16, pitch lda), b_host (K x N fp16, pitch ldb) and
  * c_host (M x N fp32, pitch ldc) are host memory (page-locked for the copies
- * to overlap); a_dev, b_dev and c_dev are the caller's device buffers for
+ * to overlap); b_host may be NULL when b_dev already holds B (replicated on
+ * the device, e.g. by a peer copy or an all-gather over NVLink, ordered
+ * before the call on `stream`).  a_dev, b_dev and c_dev are the caller's device buffers for
  * dense copies (pitches K, N and N; 16-byte aligned), so K and N must be
  * multiples of 8.  The rows of A and C are cut into blocks of rows_per_block
  * (rounded up to 256; 0 = about M / 16), and block i+1 is copied in while

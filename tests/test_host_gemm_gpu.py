@@ -108,3 +108,19 @@ def test_gemm_host_waits_for_earlier_work_on_the_stream(dev, cudair):
         kernels.gemm_host(a_h, b_h, c_h, a_d, b_d, c_d, stream=s)
     s.synchronize()
     assert np.array_equal(c_h.numpy(), want)
+
+
+def test_gemm_host_with_b_already_on_device(dev, cudair):
+    # b_host = NULL: B is taken from b_dev (replicated there beforehand), only
+    # A and C cross the host link.
+    import torch
+    from cudair import kernels
+    M, N, K = 1000, 520, 200
+    af, bf, c, want = kat(M, N, K)
+    a_h, c_h = _pinned(af, torch.float16), _pinned(c, torch.float32)
+    a_d = torch.empty(M, K, dtype=torch.float16, device=dev)
+    b_d = torch.from_numpy(bf).to(dev).half()
+    c_d = torch.empty(M, N, dtype=torch.float32, device=dev)
+    kernels.gemm_host(a_h, None, c_h, a_d, b_d, c_d, rows_per_block=256)
+    torch.cuda.synchronize()
+    assert np.array_equal(c_h.numpy(), want)
