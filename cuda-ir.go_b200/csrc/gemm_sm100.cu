@@ -543,48 +543,106 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0 && rank == 0) {
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true, issued_any = false;
-            for (int t = cluster; t < num_tiles && ok; t += num_clusters) {
-                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, status,
-                               kSiteMmaAccEmpty)) {
-                    give_up();
-                    ok = false;
-                    break;
+            // The MMAs of k-block kb (held in stage st) into the 256-column
+            // blocks [h_lo, h_hi) of accumulator acc.
+            auto issue = [&](uint32_t st, int kb, int h_lo, int h_hi) {
+                const uint32_t a_base = smem_u32(sA + st * A_BOX_BYTES);
+                const uint32_t b_base = smem_u32(sB + st * Cfg::STAGE_B);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                    for (int h = h_lo; h < h_hi; ++h) {
+                        const uint32_t b_blk = b_base + h * 2 * B_BOX_BYTES;
+                        const uint64_t b_desc =
+                            BT ? smem_desc_sw128(b_blk + kk * 32, 16, 1024)
+                               : smem_desc_sw128(b_blk + kk * 2048, B_BOX_BYTES, 1024);
+                        umma_f16_ss_pair(tmem_base + acc * 256 + h * 256, a_desc, b_desc, idesc,
+                                         (kb | kk) != 0 ? 1u : 0u);
+                    }
                 }
-                tc_fence_after_sync();
-                const uint32_t d_tmem = tmem_base + acc * 256;
-                for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, status, kSiteMmaFull)) {
-                        give_up();
-                        ok = false;
-                        break;
-                    }
+                issued_any = true;
+            };
+            // k-blocks [lo, hi) of one tile, both halves, releasing each stage.
+            auto plain = [&](int lo, int hi) -> bool {
+                for (int kb = lo; kb < hi; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, status, kSiteMmaFull)) return false;
                     tc_fence_after_sync();
-                    const uint32_t a_base = smem_u32(sA + stage * A_BOX_BYTES);
-                    const uint32_t b_base = smem_u32(sB + stage * Cfg::STAGE_B);
-#pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
-#pragma unroll
-                        for (int h = 0; h < NB; ++h) {
-                            const uint32_t b_blk = b_base + h * 2 * B_BOX_BYTES;
-                            const uint64_t b_desc =
-                                BT ? smem_desc_sw128(b_blk + kk * 32, 16, 1024)
-                                   : smem_desc_sw128(b_blk + kk * 2048, B_BOX_BYTES, 1024);
-                            umma_f16_ss_pair(d_tmem + h * 256, a_desc, b_desc, idesc,
-                                             (kb | kk) != 0 ? 1u : 0u);
-                        }
-                    }
-                    issued_any = true;
+                    issue(stage, kb, 0, NB);
                     umma_commit_pair_multicast(&empty[stage], 0x3);
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
-                if (!ok) break;
-                umma_commit_pair_multicast(&acc_full[acc], 0x3);
-                if (Cfg::ACCS == 2) acc ^= 1u;
-                if (acc == 0) acc_phase ^= 1u;
+                return true;
+            };
+            // 256 x 512 tiles: one accumulator fills TMEM, so its epilogue
+            // cannot overlap the next tile's mainloop; its two 256-column
+            // halves are handed over separately instead.  In the first and
+            // the last ring-full of k-blocks of a tile (a "window", the k-blocks
+            // all resident at once), half 0 is multiplied for every k-block
+            // before half 1.  So the tile's half 0 is finished, and its
+            // epilogue starts, while half 1's last MMAs run; and the next tile
+            // starts on half 0 while half 1 is still being drained.
+            auto window = [&](int lo, int hi, bool first, bool last) -> bool {
+                const uint32_t st0 = stage;
+                if (first) {
+                    if (!mbar_wait(&acc_empty[0], acc_phase ^ 1u, abort_flag, status, kSiteMmaAccEmpty))
+                        return false;
+                    tc_fence_after_sync();
+                }
+                for (int kb = lo; kb < hi; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, status, kSiteMmaFull)) return false;
+                    tc_fence_after_sync();
+                    issue(stage, kb, 0, 1);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (last) umma_commit_pair_multicast(&acc_full[0], 0x3);
+                if (first) {
+                    if (!mbar_wait(&acc_empty[1], acc_phase ^ 1u, abort_flag, status, kSiteMmaAccEmpty))
+                        return false;
+                    tc_fence_after_sync();
+                }
+                uint32_t st = st0;
+                for (int kb = lo; kb < hi; ++kb) {
+                    issue(st, kb, 1, 2);
+                    umma_commit_pair_multicast(&empty[st], 0x3);
+                    if (++st == STAGES) st = 0;
+                }
+                if (last) umma_commit_pair_multicast(&acc_full[1], 0x3);
+                return true;
+            };
+            for (int t = cluster; t < num_tiles && ok; t += num_clusters) {
+                if (NB == 2) {
+                    const int head_end = min(STAGES, num_kb);
+                    const int tail_lo = max(head_end, num_kb - STAGES);
+                    ok = window(0, head_end, true, head_end == num_kb) && plain(head_end, tail_lo) &&
+                         (tail_lo == num_kb || window(tail_lo, num_kb, false, true));
+                    if (!ok) {
+                        give_up();
+                        break;
+                    }
+                    acc_phase ^= 1u;
+                } else {
+                    if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, status,
+                                   kSiteMmaAccEmpty)) {
+                        give_up();
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
+                    if (!plain(0, num_kb)) {
+                        give_up();
+                        ok = false;
+                        break;
+                    }
+                    umma_commit_pair_multicast(&acc_full[acc], 0x3);
+                    acc ^= 1u;
+                    if (acc == 0) acc_phase ^= 1u;
+                }
             }
             if (!ok && issued_any) {
                 umma_commit_pair_local(drain);
@@ -603,28 +661,33 @@ __global__ void __launch_bounds__(THREADS, 1)
             tile_coords(t, num_m, num_n, P_GROUP_M, m_blk, n_blk);
             const int m0 = m_blk * P_BM + 128 * static_cast<int>(rank), n0 = n_blk * Cfg::TILE_N;
             const int row0 = m0 + static_cast<int>(q * 32);
-            if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, status,
-                           kSiteEpilogueAccFull)) {
-                give_up();
-                break;
-            }
-            tc_fence_after_sync();
-            const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * 256;
+            // 256 x 256 tiles: accumulator `acc` (of two) in one piece.  256 x
+            // 512 tiles: the one accumulator's two halves, each announced on
+            // its own acc_full and handed back on its own acc_empty.
+            bool aborted = false;
 #pragma unroll 1
             for (int h = 0; h < NB; ++h) {
+                const uint32_t bar = (NB == 2) ? static_cast<uint32_t>(h) : acc;
+                if (!mbar_wait(&acc_full[bar], acc_phase, abort_flag, status, kSiteEpilogueAccFull)) {
+                    give_up();
+                    aborted = true;
+                    break;
+                }
+                tc_fence_after_sync();
+                const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * 256 + 256 * h;
                 if (epi != kEpiScalarAdd) {
                     if (row0 < M)
-                        epilogue_rows_tma(t_row + 256 * h, &tmC, boxes, row0, n0 + 256 * h, N, cpol,
-                                          buf, epi);
+                        epilogue_rows_tma(t_row, &tmC, boxes, row0, n0 + 256 * h, N, cpol, buf, epi);
                 } else {
                     const int row = row0 + static_cast<int>(lane);
-                    epilogue_rows_scalar(t_row + 256 * h, C + static_cast<long long>(row) * ldc, row,
-                                         n0 + 256 * h, M, N);
+                    epilogue_rows_scalar(t_row, C + static_cast<long long>(row) * ldc, row, n0 + 256 * h,
+                                         M, N);
                 }
+                tc_fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[bar]), 0));
             }
-            tc_fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+            if (aborted) break;
             if (Cfg::ACCS == 2) acc ^= 1u;
             if (acc == 0) acc_phase ^= 1u;
         }
