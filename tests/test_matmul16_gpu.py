@@ -338,21 +338,27 @@ def test_gemm_c_beyond_2p31_elements(dev, cudair, variant_id):
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("M", [1, 16])
+@pytest.mark.parametrize("M", [1, 16, 40, 64])
 @pytest.mark.parametrize("kb", [2, 3, 4, 5, 6, 8, 16])
 def test_fewrows_contributors_per_tile(dev, cudair, M, kb):
     # With fewer 64-wide k-blocks than SMs, every k-block has its own CTA, so
     # each 128-column tile has exactly kb contributors; their parts must all
     # be summed, whichever contributor finishes last.  Exact (integer data),
     # twice in a row from the same C (bit-identical, timing-independent).
+    # N = 1001 in a C of pitch 1004: 16-byte aligned rows with a ragged last
+    # tile (the fix-up's staged copies of C end in a partial 16-byte piece).
     import torch
     from cudair import kernels
-    for N in (128, 264):
+    for N, ldc in ((128, 128), (264, 264), (1001, 1004)):
         K = 64 * kb
         af, bf, c, want = kat(M, N, K)
-        da, db = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16)
+        da = _dev(af, dev, torch.float16)
+        B = torch.zeros(K, (N + 7) // 8 * 8, dtype=torch.float16, device=dev)
+        B[:, :N] = _dev(bf, dev, torch.float16)
         for _ in range(2):
-            dc = _dev(c, dev, torch.float32)
-            kernels.gemm(da, db, dc)
-            got = dc.cpu().numpy()
-            assert np.array_equal(got, want), (N, K)
+            C = torch.full((M, ldc), -9.0, dtype=torch.float32, device=dev)
+            C[:, :N] = _dev(c, dev, torch.float32)
+            kernels.gemm(da, B[:, :N], C[:, :N])
+            got = C.cpu().numpy()
+            assert np.array_equal(got[:, :N], want), (N, K)
+            assert np.all(got[:, N:] == -9.0)
