@@ -281,6 +281,90 @@ class CpuGemm:
         return 2.0 * rows * N_DIM * K_DIM / dt / 1e12, rows, dt
 
 
+def run_matmul16_n256(dev, kernels):
+    """The MatMul16 parity configuration (n = 256, the reference test's size):
+    per-launch latency of the module entry under the reference's launch
+    (grid (n/16, n/16) x 32 threads) and of the tuned tcgen05 kernel, each from
+    a CUDA graph of 20 launches (a single launch timed from Python measures the
+    host's launch cost).  Inputs: fp16(U(-1,1)) A and B, U(-1,1) C."""
+    import ctypes
+
+    import torch
+    from cudair import host
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    n = 256
+    af = oracle.f16_to_f32(oracle.f32_to_f16(oracle.uniform(n * n, 1))).reshape(n, n)
+    bf = oracle.f16_to_f32(oracle.f32_to_f16(oracle.uniform(n * n, 2))).reshape(n, n)
+    c0 = oracle.uniform(n * n, 3).reshape(n, n)
+    a = torch.from_numpy(af).to(dev).half()
+    b = torch.from_numpy(bf).to(dev).half()
+    c = torch.from_numpy(c0).to(dev)
+    mod = host.LoadModule(host.KernelsImage())
+    fn = mod.Function("MatMul16")
+    cfg = host.LaunchConfig(GridX=n // 16, GridY=n // 16, BlockX=32)
+    args = (host.ArgBuffer(a), host.ArgBuffer(b), host.ArgBuffer(c), host.ArgValue(ctypes.c_int32(n)))
+    out = {}
+    for name, launch in (("reference_launch_us", lambda s: fn.LaunchExOn(s, cfg, host.LaunchAttrs(), *args)),
+                         ("tcgen05_us", lambda s: kernels.matmul16(a, b, c, stream=s))):
+        st = torch.cuda.Stream(device=dev)
+        for _ in range(3):
+            launch(st)
+        st.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for _ in range(20):
+                launch(st)
+        graph.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) / 20 * 1e3)
+        out[name] = statistics.median(ts)
+        del graph
+    mod.Close()
+    t0 = time.perf_counter()
+    oracle.gemm_ijk(af, bf, c0, threads=1)
+    out["cpu_us_1thread"] = (time.perf_counter() - t0) * 1e6
+    out["timing"] = "CUDA graph of 20 launches, per launch; CPU: the i-j-k loop, 1 thread"
+    return out
+
+
+def cpu_secondary():
+    """The reference's CPU loops for the VecAdd (2^26-element sample of the
+    2^28 workload) and decode-shaped GEMM configurations, 1 thread and all
+    host threads."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    T = oracle.num_threads()
+    out = {}
+    n = 1 << 26
+    a, b = oracle.uniform(n, 4), oracle.uniform(n, 5)
+    for t in (1, T):
+        best = float("inf")
+        for _ in range(2):  # the second call reuses the output pages the first one touched
+            t0 = time.perf_counter()
+            oracle.vecadd(a, b, threads=t)
+            best = min(best, time.perf_counter() - t0)
+        out[f"vecadd_GB/s_{'1thread' if t == 1 else 'all'}"] = 12 * n / best / 1e9
+    sm, sn, sk = SKINNY
+    af = oracle.normal(sm * sk, 9).reshape(sm, sk)
+    bf = (oracle.normal(sk * sn, 10) * 0.02).astype("float32").reshape(sk, sn)
+    c = oracle.uniform(sm * sn, 11).reshape(sm, sn) * 0
+    for t in (1, T):
+        t0 = time.perf_counter()
+        oracle.gemm_ikj(af, bf, c, threads=t)
+        out[f"skinny_ms_{'1thread' if t == 1 else 'all'}"] = (time.perf_counter() - t0) * 1e3
+    out["threads"] = T
+    out["sample"] = "VecAdd: 2^26 elements; decode GEMM: the whole 16x14336x4096 (i-k-j float32 loop)"
+    return out
+
+
 def run_reference(args, world, rank):
     """The reference arm: the CPU i-j-k loop on all host threads, rank 0 only;
     each step computes one row per thread of the workload."""
@@ -500,9 +584,12 @@ def run_ours(args, world, rank, local):
     s_ms, s_gbs = run_skinny(args, world, rank, dev, g, kernels)
     kernels.wait_status(clear=True)
 
-    # -- CPU baseline (rank 0, N = 1 only)
+    # -- the n = 256 parity configuration and the CPU baselines (rank 0, N = 1 only)
+    mm256 = run_matmul16_n256(dev, kernels) if (rank == 0 and world == 1) else None
     cpu = None
+    cpu_more = None
     if rank == 0 and world == 1 and not args.no_cpu:
+        cpu_more = cpu_secondary()
         r, rows, dt = CpuGemm(max_rows=256).sample(1, budget_s=args.cpu_budget)
         cpu = {"value": r, "unit": "TFLOP/s", "cores": 1, "kind": "port",
                "sample": f"{rows} rows of the 8192^3 C = A.B + C by the i-j-k float32 loop "
@@ -529,6 +616,8 @@ def run_ours(args, world, rank, local):
         "clocks": clocks,
         "b_replication_ms": b_ms,
         "gather": gather,
+        "matmul16_n256": mm256,
+        "cpu_secondary": cpu_more,
         "vecadd": {"value": v_gbs * world, "unit": "GB/s", "ms_per_step": v_ms, "n_per_gpu": VEC_N,
                    "roofline": {"bound": "hbm", "achieved": v_gbs, "peak": peaks["hbm_gbs"],
                                 "unit": "GB/s", "frac": v_gbs / peaks["hbm_gbs"],

@@ -75,6 +75,9 @@ int skinny_reset_workspace();
 // (cudair_set_gemm_pdl): 0 off, 1 on, 2 on with B requested early.
 int gemm_pdl_mode();
 
+// The one-warp-per-tile MatMul16 (square n, a multiple of 16; row-major, ld = n).
+int matmul16_warp_launch(const void *a, const void *b, float *c, int n, cudaStream_t stream);
+
 int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K,
                        int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t stream);
 

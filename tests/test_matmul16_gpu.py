@@ -267,10 +267,14 @@ def test_fewrows_deterministic_and_within_tolerance(dev, cudair, oracle, M, N, K
     da = torch.from_numpy(a16.view(np.int16)).to(dev).view(torch.float16).reshape(M, K)
     db = torch.from_numpy(b16.view(np.int16)).to(dev).view(torch.float16).reshape(K, N)
     outs = []
-    for _ in range(2):
-        dc = torch.from_numpy(c.copy()).to(dev)
-        kernels.gemm(da, db, dc)
-        outs.append(dc.cpu().numpy())
+    kernels.set_gemm_variant(3)  # the few-row kernel, whatever the automatic choice
+    try:
+        for _ in range(2):
+            dc = torch.from_numpy(c.copy()).to(dev)
+            kernels.gemm(da, db, dc)
+            outs.append(dc.cpu().numpy())
+    finally:
+        kernels.set_gemm_variant(0)
     assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
     want = oracle.gemm_ikj(af.reshape(M, K), bf.reshape(K, N), c)
     tol_rel, tol_max = oracle.gemm_tolerance(K, np.abs(af).max(), np.abs(bf).max())
@@ -349,16 +353,20 @@ def test_fewrows_contributors_per_tile(dev, cudair, M, kb):
     # tile (the fix-up's staged copies of C end in a partial 16-byte piece).
     import torch
     from cudair import kernels
-    for N, ldc in ((128, 128), (264, 264), (1001, 1004)):
-        K = 64 * kb
-        af, bf, c, want = kat(M, N, K)
-        da = _dev(af, dev, torch.float16)
-        B = torch.zeros(K, (N + 7) // 8 * 8, dtype=torch.float16, device=dev)
-        B[:, :N] = _dev(bf, dev, torch.float16)
-        for _ in range(2):
-            C = torch.full((M, ldc), -9.0, dtype=torch.float32, device=dev)
-            C[:, :N] = _dev(c, dev, torch.float32)
-            kernels.gemm(da, B[:, :N], C[:, :N])
-            got = C.cpu().numpy()
-            assert np.array_equal(got[:, :N], want), (N, K)
-            assert np.all(got[:, N:] == -9.0)
+    kernels.set_gemm_variant(3)  # the few-row kernel, whatever the automatic choice
+    try:
+        for N, ldc in ((128, 128), (264, 264), (1001, 1004)):
+            K = 64 * kb
+            af, bf, c, want = kat(M, N, K)
+            da = _dev(af, dev, torch.float16)
+            B = torch.zeros(K, (N + 7) // 8 * 8, dtype=torch.float16, device=dev)
+            B[:, :N] = _dev(bf, dev, torch.float16)
+            for _ in range(2):
+                C = torch.full((M, ldc), -9.0, dtype=torch.float32, device=dev)
+                C[:, :N] = _dev(c, dev, torch.float32)
+                kernels.gemm(da, B[:, :N], C[:, :N])
+                got = C.cpu().numpy()
+                assert np.array_equal(got[:, :N], want), (N, K)
+                assert np.all(got[:, N:] == -9.0)
+    finally:
+        kernels.set_gemm_variant(0)
