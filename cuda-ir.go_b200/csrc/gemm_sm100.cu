@@ -276,10 +276,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    // Programmatic dependent launch (cudair_set_gemm_pdl): every CTA is set
+    // up, so the next kernel in the stream may be launched; this one waits
+    // for the preceding kernel before it reads A, B or C (no-ops without the
+    // launch attribute).
+    if (threadIdx.x == 0) grid_launch_dependents();
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
+            grid_dependency_wait();
             const uint64_t policy = l2_policy_evict_normal();
             uint32_t stage = 0, phase = 0, issued = 0;
             bool ok = true;
@@ -373,6 +379,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
+        grid_dependency_wait();  // C may be the preceding kernel's
         const uint32_t q = warp & 3u;  // the TMEM lane quarter this warp may read
         const uint64_t cpol = c_policy();
         const uint32_t boxes = smem_u32(sEpi) + q * 2 * EPI_BOX_BYTES;
@@ -475,6 +482,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     cluster_sync();  // barriers of both CTAs initialised before any remote arrive
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    // Programmatic dependent launch: as in the single-CTA kernel.
+    if (threadIdx.x == 0) grid_launch_dependents();
 
     // A wait that gave up here also stops the peer CTA.
     auto give_up = [&]() { st_shared_cluster_u32(peer_abort, 1u); };
@@ -484,6 +493,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
         if (lane == 0) {
+            grid_dependency_wait();
             const uint64_t policy = l2_policy_evict_normal();
             uint32_t stage = 0, phase = 0;
             bool ok = true;
@@ -652,6 +662,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
     } else {
         // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+        grid_dependency_wait();  // C may be the preceding kernel's
         const uint32_t q = warp & 3u;
         const uint64_t cpol = c_policy();
         const uint32_t boxes = smem_u32(sEpi) + q * 2 * EPI_BOX_BYTES;
@@ -737,7 +748,7 @@ struct DeviceInfo {
 std::mutex g_dev_mu;
 DeviceInfo g_dev[64];
 std::atomic<int> g_variant{0};  // 0 auto, 1 single CTA, 2 CTA pair
-std::atomic<int> g_pdl{0};      // few-row GEMM: 0 plain launch, 1 PDL, 2 PDL with B early
+std::atomic<int> g_pdl{0};      // 0 plain launch, 1 PDL, 2 PDL with B early (few-row kernel)
 
 int device_info(DeviceInfo **out) {
     int dev = 0;
@@ -843,30 +854,41 @@ namespace {
 template <bool BT>
 cudaError_t launch_square(int nb, const DeviceInfo &dev, const CUtensorMap &tmA, const CUtensorMap &tmB,
                           const CUtensorMap &tmC, float *c, int64_t M, int64_t N, int64_t K,
-                          long long ldc, bool bf16, int epi, cudaStream_t stream) {
+                          long long ldc, bool bf16, int epi, bool pdl, cudaStream_t stream) {
     const int Mi = static_cast<int>(M), Ni = static_cast<int>(N), Ki = static_cast<int>(K);
     if (nb == 0) {
         const int64_t tiles = ((M + gemm::S_BM - 1) / gemm::S_BM) * ((N + gemm::BN - 1) / gemm::BN);
         const int grid = static_cast<int>(tiles < dev.sm_count ? tiles : dev.sm_count);
         const uint32_t idesc = idesc_f16_f32(gemm::S_BM, gemm::BN, false, !BT, bf16);
-        gemm::gemm_f16f32_kernel<BT><<<grid, gemm::THREADS, gemm::S_SMEM, stream>>>(
-            tmA, tmB, tmC, c, Mi, Ni, Ki, ldc, idesc, epi);
-        return cudaGetLastError();
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+        cfg.blockDim = dim3(gemm::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = gemm::S_SMEM;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 1 : 0;
+        return cudaLaunchKernelEx(&cfg, gemm::gemm_f16f32_kernel<BT>, tmA, tmB, tmC, c, Mi, Ni, Ki, ldc, idesc,
+                                  epi);
     }
     const int tile_n = 256 * nb;
     const int64_t tiles = ((M + gemm::P_BM - 1) / gemm::P_BM) * ((N + tile_n - 1) / tile_n);
     const int pairs = static_cast<int>(tiles < dev.max_pairs ? tiles : dev.max_pairs);
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(gemm::THREADS, 1, 1);
     cfg.stream = stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 2 : 1;
     const uint32_t idesc = idesc_f16_f32(gemm::P_BM, 256, false, !BT, bf16);
     if (nb == 2) {
         cfg.dynamicSmemBytes = gemm::PairCfg<2>::SMEM;
@@ -1012,10 +1034,11 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
         if (rc != CUDAIR_OK) return rc;
     }
     float *cf = static_cast<float *>(c);
+    const bool pdl = g_pdl.load() > 0;
     e = bt ? launch_square<true>(nb, *dev, tmA, tmB, tmC, cf, M, N, K, static_cast<long long>(ldc), bf16, epi,
-                                 stream)
+                                 pdl, stream)
            : launch_square<false>(nb, *dev, tmA, tmB, tmC, cf, M, N, K, static_cast<long long>(ldc), bf16,
-                                  epi, stream);
+                                  epi, pdl, stream);
     if (e != cudaSuccess) return cuda_error(e, nb ? "gemm_f16f32_pair_kernel launch" : "gemm_f16f32_kernel launch");
     return CUDAIR_OK;
 }

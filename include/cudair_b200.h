@@ -204,16 +204,18 @@ int cudair_gemm(const void *a, const void *b, void *c, const float *bias,
 int cudair_set_gemm_variant(int variant);
 
 /*
- * Programmatic dependent launch for the few-row GEMM (the
+ * Programmatic dependent launch for the GEMM kernels (the
  * ProgrammaticStreamSerialization launch attribute of the reference's
  * host.LaunchAttrs, host/launchex.go:105-148), for chains of GEMMs on one
  * stream such as a decode step.  mode 0 (default): a plain launch.  mode 1:
  * the launch may begin while the preceding kernel in the stream finishes; the
  * kernel sets up and then waits for that kernel (griddepcontrol.wait) before
- * it reads A, B, C or its workspace.  mode 2: as 1, but the first stages of B
- * are requested before the wait.  The caller promises that the preceding
- * kernel does not write B (weights).  Results are identical in all modes.
- * Applies to subsequent calls of cudair_gemm_f16f32 in this process.
+ * it reads A, B, C or its workspace.  mode 2: as 1, and the few-row kernel
+ * requests the first stages of B before the wait (the square-tile kernels
+ * treat it as 1).  The caller promises that the preceding kernel does not
+ * write B (weights).  Results are identical in all modes.  Applies to
+ * subsequent GEMM calls (cudair_gemm_f16f32, cudair_gemm, cudair_matmul16
+ * above n = 384) in this process.
  */
 int cudair_set_gemm_pdl(int mode);
 

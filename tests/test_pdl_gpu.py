@@ -88,3 +88,37 @@ def test_pdl_chain_in_cuda_graph(dev, cudair, pdl):
     torch.cuda.synchronize()
     prod = want1.astype(np.float64) - c
     assert np.array_equal(dc.cpu().numpy(), (c + 18 * prod).astype(np.float32))
+
+
+@pytest.mark.parametrize("variant", [1, 2, 4], ids=["single", "pair", "pairwide"])
+def test_pdl_square_kernel_chain(dev, cudair, pdl, variant):
+    # The square-tile kernels under programmatic dependent launch: a chain
+    # that reads an A just written by a torch kernel and adds into a C just
+    # written by the preceding GEMM, exact in every mode.
+    import torch
+    from cudair import kernels
+    M, N, K = 512, 1024, 256
+    a1, b1, da1, db1 = _ops(M, N, K, dev, 21)
+    a2, b2, _, db2 = _ops(M, N, K, dev, 22)
+    c0 = (np.arange(M * N, dtype=np.float32).reshape(M, N) % 89) - 44
+    dc = torch.from_numpy(c0).to(dev)
+    da2 = torch.zeros(M, K, dtype=torch.float16, device=dev)
+    src2 = torch.from_numpy(a2).to(dev).half()
+    torch.cuda.synchronize()
+    kernels.set_gemm_variant(variant)
+    try:
+        big = torch.randn(2048, 2048, device=dev)
+        for _ in range(3):
+            big = big @ big
+        for _ in range(3):
+            kernels.gemm(da1, db1, dc)
+        da2.copy_(src2)
+        kernels.gemm(da2, db2, dc)
+        kernels.gemm(da2, db2, dc)
+        torch.cuda.synchronize()
+    finally:
+        kernels.set_gemm_variant(0)
+    p1 = a1.astype(np.int64) @ b1.astype(np.int64)
+    p2 = a2.astype(np.int64) @ b2.astype(np.int64)
+    want = (c0.astype(np.int64) + 3 * p1 + 2 * p2).astype(np.float32)
+    assert np.array_equal(dc.cpu().numpy(), want)
