@@ -199,6 +199,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
+            // The bounded waits below time this launch's own pipeline, not
+            // the preceding kernel (A arrives only after that wait anyway).
+            grid_dependency_wait();
             const uint32_t idesc = idesc_f16_f32(BN_T, static_cast<uint32_t>(mpad), true, false);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true, issued_any = false;

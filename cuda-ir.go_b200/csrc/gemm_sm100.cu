@@ -330,6 +330,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
+            // The bounded waits below time this launch's own pipeline, not
+            // the preceding kernel (operands arrive only after that wait).
+            grid_dependency_wait();
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true, issued_any = false;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -551,6 +554,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (even CTA) ----------------
         if (lane == 0 && rank == 0) {
+            grid_dependency_wait();  // as in the single-CTA kernel
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true, issued_any = false;
             // The MMAs of k-block kb (held in stage st) into the 256-column
