@@ -13,18 +13,13 @@ namespace {
 
 constexpr int kStreamThreads = 512;
 
-// The persistent grid of the streaming kernels (VecAdd, Saxpy, Square): 4
-// CTAs of 512 threads per SM (every SM kept at full occupancy, 16 loads of 16
-// bytes in flight per thread pair), capped by the work so small n does not
-// launch idle CTAs.
-int stream_grid(int32_t n, unsigned *blocks_out) {
-    int sms = 0;
-    int rc = sm_count_current_device(&sms);
-    if (rc != CUDAIR_OK) return rc;
+// The grid of the streaming kernels (VecAdd, Saxpy, Square): one chunk of
+// 512 x V 16-byte vectors per block (V = vectors per thread: 1 for VecAdd and
+// Saxpy, 2 for Square), as many blocks as chunks.
+int stream_grid(int32_t n, int vectors_per_thread, unsigned *blocks_out) {
     const int64_t vec_work = (static_cast<int64_t>(n) + 3) / 4;
-    int64_t blocks = (vec_work + kStreamThreads - 1) / kStreamThreads;
-    const int64_t cap = static_cast<int64_t>(sms) * 4;
-    if (blocks > cap) blocks = cap;
+    const int64_t chunk = static_cast<int64_t>(kStreamThreads) * vectors_per_thread;
+    int64_t blocks = (vec_work + chunk - 1) / chunk;
     if (blocks < 1) blocks = 1;
     *blocks_out = static_cast<unsigned>(blocks);
     return CUDAIR_OK;
@@ -38,7 +33,7 @@ CUDAIR_API int cudair_vecadd(const float *a, const float *b, float *out, int32_t
     if (n == 0) return CUDAIR_OK;
     if (!a || !b || !out) return set_error(CUDAIR_ERR_INVALID, "cudair: VecAdd: nil pointer");
     unsigned blocks = 0;
-    int rc = stream_grid(n, &blocks);
+    int rc = stream_grid(n, cudair_detail::kVecAddV, &blocks);
     if (rc != CUDAIR_OK) return rc;
     VecAdd<<<blocks, kStreamThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, b, out, n);
     cudaError_t e = cudaGetLastError();
@@ -63,7 +58,7 @@ CUDAIR_API int cudair_saxpy(float alpha, const float *x, float *y, int32_t n, vo
     if (n == 0) return CUDAIR_OK;
     if (!x || !y) return set_error(CUDAIR_ERR_INVALID, "cudair: Saxpy: nil pointer");
     unsigned blocks = 0;
-    int rc = stream_grid(n, &blocks);
+    int rc = stream_grid(n, cudair_detail::kVecAddV, &blocks);
     if (rc != CUDAIR_OK) return rc;
     Saxpy<<<blocks, kStreamThreads, 0, static_cast<cudaStream_t>(stream)>>>(alpha, x, y, n);
     cudaError_t e = cudaGetLastError();
@@ -77,7 +72,7 @@ CUDAIR_API int cudair_square(float *x, int32_t n, void *stream) {
     if (n == 0) return CUDAIR_OK;
     if (!x) return set_error(CUDAIR_ERR_INVALID, "cudair: Square: nil pointer");
     unsigned blocks = 0;
-    int rc = stream_grid(n, &blocks);
+    int rc = stream_grid(n, cudair_detail::kSquareV, &blocks);
     if (rc != CUDAIR_OK) return rc;
     Square<<<blocks, kStreamThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, n);
     cudaError_t e = cudaGetLastError();

@@ -11,20 +11,99 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+// ---- Streaming helper (VecAdd, Saxpy, Square) ----------------------------------
+
+namespace cudair_detail {
+
+// out[i] = f(in0[i] (, in1[i])) over n4 16-byte vectors, in chunks of
+// blockDim.x * V vectors: block b takes chunks b, b + gridDim.x, ..., and
+// thread t of a block the vectors t, t + blockDim.x, ... of its chunk, so
+// every warp access is coalesced and all of a thread's loads are issued
+// before its stores.  Under the library's launch (one chunk per block, many
+// blocks) the hardware hands chunks to SMs as they finish, so SMs that get
+// more bandwidth stream more; a persistent grid-stride split fixes every
+// SM's share in advance and ends with the slowest one (VecAdd at 2^28:
+// 0.50 against 0.455 ms).  Under any other launch the loop still covers all
+// vectors.  Streaming (evict-first) cache policy: every byte is touched once.
+template <int V, int NIN, class F>
+__device__ __forceinline__ void stream_chunks(const float4 *in0, const float4 *in1, float4 *out,
+                                              int64_t n4, F f) {
+    // n4 < 2^29 (n is an int32), so every vector index inside a chunk fits
+    // 32 bits; only the chunk cursor, whose stride can be huge under an
+    // arbitrary launch, is kept in 64.
+    const uint32_t T = blockDim.x, chunk = T * V;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * chunk;
+    for (uint64_t c0 = static_cast<uint64_t>(blockIdx.x) * chunk; c0 < static_cast<uint64_t>(n4); c0 += stride) {
+        const uint32_t i = static_cast<uint32_t>(c0) + threadIdx.x;
+        float4 x[V], y[V];
+        if (c0 + chunk <= static_cast<uint64_t>(n4)) {
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                x[k] = __ldcs(in0 + (i + k * T));
+                if constexpr (NIN == 2) y[k] = __ldcs(in1 + (i + k * T));
+            }
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                if constexpr (NIN == 2) __stcs(out + (i + k * T), f(x[k], y[k]));
+                else __stcs(out + (i + k * T), f(x[k]));
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                const uint32_t j = i + k * T;
+                if (j < static_cast<uint64_t>(n4)) {
+                    x[k] = __ldcs(in0 + j);
+                    if constexpr (NIN == 2) {
+                        y[k] = __ldcs(in1 + j);
+                        __stcs(out + j, f(x[k], y[k]));
+                    } else {
+                        __stcs(out + j, f(x[k]));
+                    }
+                }
+            }
+        }
+    }
+}
+
+// Vectors per thread and chunk: two 16-byte loads in flight per thread (at
+// 2048 threads per SM, 64 KB per SM), the fastest of 1/2/4/8 at 128-512
+// threads per block.
+constexpr int kVecAddV = 1;  // two inputs
+constexpr int kSquareV = 2;  // one input
+
+struct AddOp {
+    __device__ __forceinline__ float4 operator()(const float4 &a, const float4 &b) const {
+        return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+    }
+};
+struct SaxpyOp {
+    float alpha;
+    __device__ __forceinline__ float4 operator()(const float4 &x, const float4 &y) const {
+        return make_float4(__fadd_rn(__fmul_rn(alpha, x.x), y.x), __fadd_rn(__fmul_rn(alpha, x.y), y.y),
+                           __fadd_rn(__fmul_rn(alpha, x.z), y.z), __fadd_rn(__fmul_rn(alpha, x.w), y.w));
+    }
+};
+struct SquareOp {
+    __device__ __forceinline__ float4 operator()(const float4 &x) const {
+        return make_float4(__fmul_rn(x.x, x.x), __fmul_rn(x.y, x.y), __fmul_rn(x.z, x.z), __fmul_rn(x.w, x.w));
+    }
+};
+
+}  // namespace cudair_detail
+
 // ---- VecAdd -----------------------------------------------------------------
 
 // out[i] = a[i] + b[i] for i < n.  examples/vecadd/vecadd.go:6-11.
 //
 // The reference gives each thread one scalar element (launched
-// LaunchConfig1D(n, 256), main_test.go:37).  Here every thread walks a
-// grid-stride loop over 16-byte vectors, four vectors per trip with all loads
-// issued before the adds, so the same entry is correct under that launch (most
-// threads then find no work) and saturates HBM under a persistent launch of a
-// few CTAs per SM.  Loads and stores use the streaming (evict-first) cache
-// policy: every byte is touched once.  When the three pointers do not share
-// their offset within 16 bytes the loop falls back to scalar accesses.  The
-// add is IEEE round-to-nearest, bit-exact with the CPU's float32 add.
-extern "C" __global__ void __launch_bounds__(1024)
+// LaunchConfig1D(n, 256), main_test.go:37).  Here the 16-byte-aligned middle
+// of the arrays streams in chunks of 16-byte vectors (stream_chunks above),
+// with a few scalar elements before and after it, so the same entry is
+// correct under that launch and saturates HBM under the library's launch of
+// one 512-vector chunk per block.  When the three pointers do not share their
+// offset within 16 bytes every element is done by a scalar loop.  The add is
+// IEEE round-to-nearest, bit-exact with the CPU's float32 add.
+extern "C" __global__ void __launch_bounds__(1024, 2)
     VecAdd(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ out,
            int n) {
     if (n <= 0) return;
@@ -35,41 +114,12 @@ extern "C" __global__ void __launch_bounds__(1024)
         (reinterpret_cast<uintptr_t>(b) & 15u) == mis && (mis & 3u) == 0) {
         int64_t head = static_cast<int64_t>((16u - mis) & 15u) >> 2;  // scalars before 16B
         if (head > n) head = n;
-        if (tid < head) out[tid] = __fadd_rn(a[tid], b[tid]);
+        for (int64_t j = tid; j < head; j += nthr) out[j] = __fadd_rn(a[j], b[j]);
         const int64_t n4 = (n - head) >> 2;
-        const float4 *a4 = reinterpret_cast<const float4 *>(a + head);
-        const float4 *b4 = reinterpret_cast<const float4 *>(b + head);
-        float4 *o4 = reinterpret_cast<float4 *>(out + head);
-        constexpr int U = 4;
-        int64_t i = tid;
-        for (; i + (U - 1) * nthr < n4; i += U * nthr) {
-            float4 va[U], vb[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                va[u] = __ldcs(a4 + i + u * nthr);
-                vb[u] = __ldcs(b4 + i + u * nthr);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                float4 r;
-                r.x = __fadd_rn(va[u].x, vb[u].x);
-                r.y = __fadd_rn(va[u].y, vb[u].y);
-                r.z = __fadd_rn(va[u].z, vb[u].z);
-                r.w = __fadd_rn(va[u].w, vb[u].w);
-                __stcs(o4 + i + u * nthr, r);
-            }
-        }
-        for (; i < n4; i += nthr) {
-            const float4 va = __ldcs(a4 + i), vb = __ldcs(b4 + i);
-            float4 r;
-            r.x = __fadd_rn(va.x, vb.x);
-            r.y = __fadd_rn(va.y, vb.y);
-            r.z = __fadd_rn(va.z, vb.z);
-            r.w = __fadd_rn(va.w, vb.w);
-            __stcs(o4 + i, r);
-        }
-        const int64_t t = head + 4 * n4 + tid;  // at most 3 trailing scalars
-        if (t < n) out[t] = __fadd_rn(a[t], b[t]);
+        cudair_detail::stream_chunks<cudair_detail::kVecAddV, 2>(
+            reinterpret_cast<const float4 *>(a + head), reinterpret_cast<const float4 *>(b + head),
+            reinterpret_cast<float4 *>(out + head), n4, cudair_detail::AddOp{});
+        for (int64_t t = head + 4 * n4 + tid; t < n; t += nthr) out[t] = __fadd_rn(a[t], b[t]);
     } else {
         for (int64_t i = tid; i < n; i += nthr) out[i] = __fadd_rn(a[i], b[i]);
     }
@@ -78,12 +128,11 @@ extern "C" __global__ void __launch_bounds__(1024)
 // ---- Saxpy, Square (the rest of the vecadd package) ------------------------------
 
 // y[i] = alpha * x[i] + y[i] for i < n (examples/vecadd/vecadd.go:13-18),
-// streamed like VecAdd: 16-byte vectors, four per trip with every load issued
-// first, streaming cache policy, scalar head and tail, and a scalar loop when
-// x and y do not share their offset within 16 bytes.  The product and the sum
-// are rounded separately (no fused multiply-add), as the reference's CPU check
-// computes them (vecadd/run/main.go:62-69).
-extern "C" __global__ void __launch_bounds__(1024)
+// streamed like VecAdd (scalar head and tail, 16-byte chunks between, a
+// scalar loop when x and y do not share their offset within 16 bytes).  The
+// product and the sum are rounded separately (no fused multiply-add), as the
+// reference's CPU check computes them (vecadd/run/main.go:62-69).
+extern "C" __global__ void __launch_bounds__(1024, 2)
     Saxpy(float alpha, const float *__restrict__ x, float *__restrict__ y, int n) {
     if (n <= 0) return;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -92,40 +141,12 @@ extern "C" __global__ void __launch_bounds__(1024)
     if ((reinterpret_cast<uintptr_t>(x) & 15u) == mis && (mis & 3u) == 0) {
         int64_t head = static_cast<int64_t>((16u - mis) & 15u) >> 2;
         if (head > n) head = n;
-        if (tid < head) y[tid] = __fadd_rn(__fmul_rn(alpha, x[tid]), y[tid]);
+        for (int64_t j = tid; j < head; j += nthr) y[j] = __fadd_rn(__fmul_rn(alpha, x[j]), y[j]);
         const int64_t n4 = (n - head) >> 2;
-        const float4 *x4 = reinterpret_cast<const float4 *>(x + head);
-        float4 *y4 = reinterpret_cast<float4 *>(y + head);
-        constexpr int U = 4;
-        int64_t i = tid;
-        for (; i + (U - 1) * nthr < n4; i += U * nthr) {
-            float4 vx[U], vy[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                vx[u] = __ldcs(x4 + i + u * nthr);
-                vy[u] = __ldcs(y4 + i + u * nthr);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                float4 r;
-                r.x = __fadd_rn(__fmul_rn(alpha, vx[u].x), vy[u].x);
-                r.y = __fadd_rn(__fmul_rn(alpha, vx[u].y), vy[u].y);
-                r.z = __fadd_rn(__fmul_rn(alpha, vx[u].z), vy[u].z);
-                r.w = __fadd_rn(__fmul_rn(alpha, vx[u].w), vy[u].w);
-                __stcs(y4 + i + u * nthr, r);
-            }
-        }
-        for (; i < n4; i += nthr) {
-            const float4 vx = __ldcs(x4 + i), vy = __ldcs(y4 + i);
-            float4 r;
-            r.x = __fadd_rn(__fmul_rn(alpha, vx.x), vy.x);
-            r.y = __fadd_rn(__fmul_rn(alpha, vx.y), vy.y);
-            r.z = __fadd_rn(__fmul_rn(alpha, vx.z), vy.z);
-            r.w = __fadd_rn(__fmul_rn(alpha, vx.w), vy.w);
-            __stcs(y4 + i, r);
-        }
-        const int64_t t = head + 4 * n4 + tid;
-        if (t < n) y[t] = __fadd_rn(__fmul_rn(alpha, x[t]), y[t]);
+        cudair_detail::stream_chunks<cudair_detail::kVecAddV, 2>(
+            reinterpret_cast<const float4 *>(x + head), reinterpret_cast<const float4 *>(y + head),
+            reinterpret_cast<float4 *>(y + head), n4, cudair_detail::SaxpyOp{alpha});
+        for (int64_t t = head + 4 * n4 + tid; t < n; t += nthr) y[t] = __fadd_rn(__fmul_rn(alpha, x[t]), y[t]);
     } else {
         for (int64_t i = tid; i < n; i += nthr) y[i] = __fadd_rn(__fmul_rn(alpha, x[i]), y[i]);
     }
@@ -133,7 +154,7 @@ extern "C" __global__ void __launch_bounds__(1024)
 
 // x[i] = x[i] * x[i] in place (vecadd.go:20-28; the reference gives each
 // thread one element), streamed like VecAdd.
-extern "C" __global__ void __launch_bounds__(1024) Square(float *__restrict__ x, int n) {
+extern "C" __global__ void __launch_bounds__(1024, 2) Square(float *__restrict__ x, int n) {
     if (n <= 0) return;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -141,32 +162,11 @@ extern "C" __global__ void __launch_bounds__(1024) Square(float *__restrict__ x,
     if ((mis & 3u) == 0) {
         int64_t head = static_cast<int64_t>((16u - mis) & 15u) >> 2;
         if (head > n) head = n;
-        if (tid < head) x[tid] = __fmul_rn(x[tid], x[tid]);
+        for (int64_t j = tid; j < head; j += nthr) x[j] = __fmul_rn(x[j], x[j]);
         const int64_t n4 = (n - head) >> 2;
         float4 *x4 = reinterpret_cast<float4 *>(x + head);
-        constexpr int U = 4;
-        int64_t i = tid;
-        for (; i + (U - 1) * nthr < n4; i += U * nthr) {
-            float4 v[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) v[u] = __ldcs(x4 + i + u * nthr);
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                float4 r;
-                r.x = __fmul_rn(v[u].x, v[u].x);
-                r.y = __fmul_rn(v[u].y, v[u].y);
-                r.z = __fmul_rn(v[u].z, v[u].z);
-                r.w = __fmul_rn(v[u].w, v[u].w);
-                __stcs(x4 + i + u * nthr, r);
-            }
-        }
-        for (; i < n4; i += nthr) {
-            const float4 v = __ldcs(x4 + i);
-            __stcs(x4 + i, make_float4(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y), __fmul_rn(v.z, v.z),
-                                       __fmul_rn(v.w, v.w)));
-        }
-        const int64_t t = head + 4 * n4 + tid;
-        if (t < n) x[t] = __fmul_rn(x[t], x[t]);
+        cudair_detail::stream_chunks<cudair_detail::kSquareV, 1>(x4, nullptr, x4, n4, cudair_detail::SquareOp{});
+        for (int64_t t = head + 4 * n4 + tid; t < n; t += nthr) x[t] = __fmul_rn(x[t], x[t]);
     } else {
         for (int64_t i = tid; i < n; i += nthr) x[i] = __fmul_rn(x[i], x[i]);
     }
