@@ -435,13 +435,15 @@ def run_e2e(args, world, rank, dev, a, b, c, flops, kernels):
 
         b_bytes = b_part.numel() * 2
         api = ("B: 1/world of its rows per rank over the host link, all-gathered over NVLink; "
-               "then cudair_gemm_f16f32_host (row blocks of 512: H2D, GEMM and D2H overlapped)")
+               "then cudair_gemm_f16f32_host (row blocks of 512: H2D, GEMM and D2H overlapped; "
+               "B is already on the device)")
     else:
         def e2e_step():
             kernels.gemm_host(a_h, b_h, c_h, a_d, b_d, c_d)
 
         b_bytes = b_h.numel() * 2
-        api = "cudair_gemm_f16f32_host (row blocks of 512: H2D, GEMM and D2H overlapped)"
+        api = ("cudair_gemm_f16f32_host (4 x 4 tiles of 2048 x 2048: B by column blocks, A by row "
+               "blocks, C by tiles; H2D, GEMM and D2H overlapped)")
 
     steps = max(3, min(args.steps, 20))
     ms = time_steps(e2e_step, steps, 3, world, dev)

@@ -2,14 +2,21 @@
 // MatMul16 test (advanced_test.go:466-483: copy A, B and C to the device,
 // launch, copy C back) as one call whose copies overlap the GEMM.
 //
-// The rows of A and C are cut into blocks.  Three streams carry the work:
-//   in       H2D of B, then of each block of A and C, in order;
-//   caller   the GEMM of block i once B and block i have landed;
-//   out      D2H of block i of C once its GEMM is done.
-// So block i+1 crosses the host link while block i is multiplied and block
-// i-1 travels back: the step costs about its H2D bytes at link speed instead
-// of H2D + GEMM + D2H in series.  The caller's stream waits for the last copy
-// out, so synchronising that stream covers the whole call.
+// C is cut into tiles of rows x columns.  Three streams carry the work:
+//   in       H2D, in order: for each column block j, the columns of B it
+//            needs, then for each row block i the rows of A (on the first
+//            column pass only) and tile (i, j) of C;
+//   caller   the GEMM of tile (i, j) once its inputs have landed;
+//   out      D2H of tile (i, j) of C once its GEMM is done.
+// So tile t+1 crosses the host link while tile t is multiplied and tile t-1
+// travels back, and the step costs about its bytes at the link's duplex
+// speed instead of H2D + GEMM + D2H in series.  Tiles in both dimensions
+// matter when B comes from the host: the first tile of C can return after
+// one column block of B and one row block of A (at 8192^3 with 2048 x 2048
+// tiles, 80 MiB) instead of after all of B, so the copies out start early
+// and the step takes the link's duplex time (8192^3: 11.66 -> 10.93 ms of
+// copies).  The caller's stream waits for the last copy out, so
+// synchronising that stream covers the whole call.
 //
 // The caller owns every buffer; the library keeps two streams and a set of
 // events per device, created on first use.
@@ -26,7 +33,7 @@ constexpr int kMaxBlocks = 64;
 
 struct HostPipe {
     cudaStream_t in = nullptr, out = nullptr;
-    cudaEvent_t start = nullptr, b_in = nullptr;
+    cudaEvent_t start = nullptr;
     cudaEvent_t block_in[kMaxBlocks], block_done[kMaxBlocks], block_out[kMaxBlocks];
     bool ready = false;
 };
@@ -52,7 +59,6 @@ int pipe_for_current_device(HostPipe **out) {
         if ((e = cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking)) != cudaSuccess)
             return cuda_error(e, "cudaStreamCreateWithFlags");
         int rc = make_event(&p.start);
-        if (rc == CUDAIR_OK) rc = make_event(&p.b_in);
         for (int i = 0; i < kMaxBlocks && rc == CUDAIR_OK; ++i) {
             rc = make_event(&p.block_in[i]);
             if (rc == CUDAIR_OK) rc = make_event(&p.block_done[i]);
@@ -103,14 +109,26 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
     if (rows_per_block < 0)
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_host: rows_per_block = %lld",
                          (long long)rows_per_block);
-    // Blocks of whole 256-row pair tiles, at most kMaxBlocks of them; by
-    // default about sixteen, so the copy out of the last block (the part of
-    // the call nothing overlaps) stays short.
-    int64_t rb = rows_per_block;
-    if (rb == 0) rb = (M + 15) / 16;
+    // Tiles of whole 256-row pair tiles.  By default, with B from the host
+    // and N >= 4096, about 4 x 4 tiles (the first copy out starts early);
+    // otherwise full-width row blocks, about sixteen, so the copy out of the
+    // last block (the part of the call nothing overlaps) stays short.  An
+    // explicit rows_per_block asks for full-width row blocks of that height.
+    // At most kMaxBlocks tiles.
+    int64_t rb = rows_per_block, cb = N;
+    if (rb == 0) {
+        if (b_host && K > 0 && N >= 4096 && M >= 1024) {
+            rb = (M + 3) / 4;
+            cb = ((N + 3) / 4 + 255) / 256 * 256;
+        } else {
+            rb = (M + 15) / 16;
+        }
+    }
     rb = (rb + 255) / 256 * 256;
-    if ((M + rb - 1) / rb > kMaxBlocks) rb = ((M + kMaxBlocks - 1) / kMaxBlocks + 255) / 256 * 256;
-    const int blocks = static_cast<int>((M + rb - 1) / rb);
+    const int col_blocks = static_cast<int>((N + cb - 1) / cb);
+    if ((M + rb - 1) / rb * col_blocks > kMaxBlocks)
+        rb = ((M + kMaxBlocks / col_blocks - 1) / (kMaxBlocks / col_blocks) + 255) / 256 * 256;
+    const int row_blocks = static_cast<int>((M + rb - 1) / rb);
 
     int rc = ensure_context();
     if (rc != CUDAIR_OK) return rc;
@@ -131,40 +149,47 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
     CUDAIR_TRY(cudaStreamWaitEvent(p->out, p->start, 0), "cudaStreamWaitEvent");
     const size_t a_row = static_cast<size_t>(K) * 2, b_row = static_cast<size_t>(N) * 2,
                  c_row = static_cast<size_t>(N) * 4;
-    if (K > 0 && b_host) {
-        CUDAIR_TRY(copy_rows(b_dev, b_row, b_host, static_cast<size_t>(ldb) * 2, b_row,
-                             static_cast<size_t>(K), cudaMemcpyHostToDevice, p->in),
-                   "H2D of B");
-        CUDAIR_TRY(cudaEventRecord(p->b_in, p->in), "cudaEventRecord");
-        CUDAIR_TRY(cudaStreamWaitEvent(s, p->b_in, 0), "cudaStreamWaitEvent");
-    }
-    for (int i = 0; i < blocks; ++i) {
-        const int64_t r0 = i * rb, rows = (M - r0 < rb) ? M - r0 : rb;
-        uint8_t *a_blk = static_cast<uint8_t *>(a_dev) + static_cast<size_t>(r0) * a_row;
-        float *c_blk = c_dev + static_cast<size_t>(r0) * N;
-        if (K > 0)
-            CUDAIR_TRY(copy_rows(a_blk, a_row,
-                                 static_cast<const uint8_t *>(a_host) + static_cast<size_t>(r0) * lda * 2,
-                                 static_cast<size_t>(lda) * 2, a_row, static_cast<size_t>(rows),
+    int t = 0;
+    for (int j = 0; j < col_blocks; ++j) {
+        const int64_t n0 = j * cb, cols = (N - n0 < cb) ? N - n0 : cb;
+        if (K > 0 && b_host)
+            CUDAIR_TRY(copy_rows(static_cast<uint8_t *>(b_dev) + static_cast<size_t>(n0) * 2, b_row,
+                                 static_cast<const uint8_t *>(b_host) + static_cast<size_t>(n0) * 2,
+                                 static_cast<size_t>(ldb) * 2, static_cast<size_t>(cols) * 2,
+                                 static_cast<size_t>(K), cudaMemcpyHostToDevice, p->in),
+                       "H2D of B");
+        for (int i = 0; i < row_blocks; ++i, ++t) {
+            const int64_t r0 = i * rb, rows = (M - r0 < rb) ? M - r0 : rb;
+            uint8_t *a_blk = static_cast<uint8_t *>(a_dev) + static_cast<size_t>(r0) * a_row;
+            float *c_tile = c_dev + static_cast<size_t>(r0) * N + n0;
+            float *c_host_tile = c_host + static_cast<size_t>(r0) * ldc + n0;
+            if (K > 0 && j == 0)
+                CUDAIR_TRY(copy_rows(a_blk, a_row,
+                                     static_cast<const uint8_t *>(a_host) + static_cast<size_t>(r0) * lda * 2,
+                                     static_cast<size_t>(lda) * 2, a_row, static_cast<size_t>(rows),
+                                     cudaMemcpyHostToDevice, p->in),
+                           "H2D of a block of A");
+            CUDAIR_TRY(copy_rows(c_tile, c_row, c_host_tile, static_cast<size_t>(ldc) * 4,
+                                 static_cast<size_t>(cols) * 4, static_cast<size_t>(rows),
                                  cudaMemcpyHostToDevice, p->in),
-                       "H2D of a block of A");
-        CUDAIR_TRY(copy_rows(c_blk, c_row, c_host + static_cast<size_t>(r0) * ldc,
-                             static_cast<size_t>(ldc) * 4, c_row, static_cast<size_t>(rows),
-                             cudaMemcpyHostToDevice, p->in),
-                   "H2D of a block of C");
-        CUDAIR_TRY(cudaEventRecord(p->block_in[i], p->in), "cudaEventRecord");
-        CUDAIR_TRY(cudaStreamWaitEvent(s, p->block_in[i], 0), "cudaStreamWaitEvent");
-        rc = gemm_f16f32_launch(a_blk, b_dev, c_blk, rows, N, K, K, N, N, s);
-        if (rc != CUDAIR_OK) return rc;
-        CUDAIR_TRY(cudaEventRecord(p->block_done[i], s), "cudaEventRecord");
-        CUDAIR_TRY(cudaStreamWaitEvent(p->out, p->block_done[i], 0), "cudaStreamWaitEvent");
-        CUDAIR_TRY(copy_rows(c_host + static_cast<size_t>(r0) * ldc, static_cast<size_t>(ldc) * 4,
-                             c_blk, c_row, c_row, static_cast<size_t>(rows), cudaMemcpyDeviceToHost,
-                             p->out),
-                   "D2H of a block of C");
-        CUDAIR_TRY(cudaEventRecord(p->block_out[i], p->out), "cudaEventRecord");
+                       "H2D of a tile of C");
+            // Everything the tile's GEMM reads (B's columns, A's rows, the
+            // tile of C) was copied earlier on the in-stream.
+            CUDAIR_TRY(cudaEventRecord(p->block_in[t], p->in), "cudaEventRecord");
+            CUDAIR_TRY(cudaStreamWaitEvent(s, p->block_in[t], 0), "cudaStreamWaitEvent");
+            rc = gemm_f16f32_launch(a_blk, static_cast<uint8_t *>(b_dev) + static_cast<size_t>(n0) * 2, c_tile,
+                                    rows, cols, K, K, N, N, s);
+            if (rc != CUDAIR_OK) return rc;
+            CUDAIR_TRY(cudaEventRecord(p->block_done[t], s), "cudaEventRecord");
+            CUDAIR_TRY(cudaStreamWaitEvent(p->out, p->block_done[t], 0), "cudaStreamWaitEvent");
+            CUDAIR_TRY(copy_rows(c_host_tile, static_cast<size_t>(ldc) * 4, c_tile, c_row,
+                                 static_cast<size_t>(cols) * 4, static_cast<size_t>(rows),
+                                 cudaMemcpyDeviceToHost, p->out),
+                       "D2H of a tile of C");
+            CUDAIR_TRY(cudaEventRecord(p->block_out[t], p->out), "cudaEventRecord");
+        }
     }
-    CUDAIR_TRY(cudaStreamWaitEvent(s, p->block_out[blocks - 1], 0), "cudaStreamWaitEvent");
+    CUDAIR_TRY(cudaStreamWaitEvent(s, p->block_out[t - 1], 0), "cudaStreamWaitEvent");
 #undef CUDAIR_TRY
     return CUDAIR_OK;
 }

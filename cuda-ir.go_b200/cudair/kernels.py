@@ -95,9 +95,10 @@ def gemm_ex(a, b, c, bias=None, b_trans=False, overwrite=False, stream=None) -> 
 def gemm_host(a_h, b_h, c_h, a_d, b_d, c_d, rows_per_block=0, stream=None) -> None:
     """c_h += a_h @ b_h from host (CPU) tensors, through the caller's device
     buffers a_d, b_d, c_d (dense, same shapes): copies in, GEMM and copy out
-    pipelined over row blocks.  b_h = None: b_d already holds B.  Asynchronous on `stream`; c_h holds the result
-    once the stream is synchronised.  Pinned host tensors let the copies
-    overlap."""
+    pipelined over tiles of C (rows_per_block > 0: full-width row blocks of
+    that height; 0: automatic).  b_h = None: b_d already holds B.
+    Asynchronous on `stream`; c_h holds the result once the stream is
+    synchronised.  Pinned host tensors let the copies overlap."""
     import torch
     for t, dt, nm in ((a_h, torch.float16, "a_h"), (b_h, torch.float16, "b_h"),
                       (c_h, torch.float32, "c_h")):

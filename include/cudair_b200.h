@@ -229,10 +229,13 @@ int cudair_set_gemm_pdl(int mode);
  * the device, e.g. by a peer copy or an all-gather over NVLink, ordered
  * before the call on `stream`).  a_dev, b_dev and c_dev are the caller's device buffers for
  * dense copies (pitches K, N and N; 16-byte aligned), so K and N must be
- * multiples of 8.  The rows of A and C are cut into blocks of rows_per_block
- * (rounded up to 256; 0 = about M / 16), and block i+1 is copied in while
- * block i is multiplied (cudair_gemm_f16f32, the automatic choice) and block
- * i-1 is copied out, on two library-owned streams per device.  The call is
+ * multiples of 8.  C is cut into tiles, and tile t+1 is copied in while tile
+ * t is multiplied (cudair_gemm_f16f32, the automatic choice) and tile t-1 is
+ * copied out, on two library-owned streams per device.  rows_per_block > 0
+ * gives full-width row blocks of that many rows (rounded up to 256).  With 0,
+ * B from the host, N >= 4096 and M >= 1024, C is cut into about 4 x 4 tiles:
+ * B then crosses the link one column block at a time, so the first tile can
+ * travel back early.  Otherwise 0 gives about 16 full-width row blocks.  The call is
  * asynchronous: `stream` waits for the last copy out, so synchronising it
  * means C is back in c_host.  Allocates nothing.
  */

@@ -124,3 +124,74 @@ def test_gemm_host_with_b_already_on_device(dev, cudair):
     kernels.gemm_host(a_h, None, c_h, a_d, b_d, c_d, rows_per_block=256)
     torch.cuda.synchronize()
     assert np.array_equal(c_h.numpy(), want)
+
+
+# With B from the host, N >= 4096 and M >= 1024, the default schedule tiles C
+# in both dimensions (about 4 x 4 tiles): B crosses the link one column block
+# at a time, A one row block at a time on the first column pass.
+
+@pytest.mark.parametrize("M,N,K", [(1100, 4104, 72), (1024, 4096, 200), (2000, 8192, 16)])
+def test_gemm_host_2d_tiles_kat_exact(dev, cudair, M, N, K):
+    # Ragged in both dimensions (1100 rows in blocks of 512; 4104 columns in
+    # blocks of 1280, the last 264 wide).
+    import torch
+    from cudair import kernels
+    af, bf, c, want = kat(M, N, K)
+    a_h, b_h, c_h = _pinned(af, torch.float16), _pinned(bf, torch.float16), _pinned(c, torch.float32)
+    a_d = torch.empty(M, K, dtype=torch.float16, device=dev)
+    b_d = torch.empty(K, N, dtype=torch.float16, device=dev)
+    c_d = torch.empty(M, N, dtype=torch.float32, device=dev)
+    kernels.gemm_host(a_h, b_h, c_h, a_d, b_d, c_d)
+    torch.cuda.synchronize()
+    assert np.array_equal(c_h.numpy(), want)
+    # The device copies hold the operands and the result, as after the
+    # reference test's copy-in / launch.
+    assert np.array_equal(c_d.cpu().numpy(), want)
+    assert torch.equal(b_d.cpu(), b_h)
+
+
+def test_gemm_host_2d_tiles_padded_pitches_and_pageable(dev, cudair):
+    import torch
+    from cudair import kernels
+    M, N, K = 1030, 4360, 136
+    af, bf, c, want = kat(M, N, K)
+    A = torch.full((M, K + 8), 9.0, dtype=torch.float16)
+    B = torch.full((K, N + 16), 9.0, dtype=torch.float16)
+    C = torch.full((M, N + 3), -2.0, dtype=torch.float32)
+    A[:, :K] = torch.from_numpy(af).half()
+    B[:, :N] = torch.from_numpy(bf).half()
+    C[:, :N] = torch.from_numpy(c)
+    a_d = torch.empty(M, K, dtype=torch.float16, device=dev)
+    b_d = torch.empty(K, N, dtype=torch.float16, device=dev)
+    c_d = torch.empty(M, N, dtype=torch.float32, device=dev)
+    kernels.gemm_host(A[:, :K], B[:, :N], C[:, :N], a_d, b_d, c_d)
+    torch.cuda.synchronize()
+    got = C.numpy()
+    assert np.array_equal(got[:, :N], want)
+    assert np.all(got[:, N:] == -2.0)
+
+
+def test_gemm_host_2d_tiles_match_device_call(dev, cudair, oracle):
+    # Seeded data at 4096^3: the tiled host call agrees with one device-buffer
+    # GEMM of the whole problem within the GEMM tolerance (each tile is
+    # computed by the same kernels over the whole K).
+    import torch
+    from cudair import kernels
+    M = N = K = 4096
+    a16, _ = _seeded_normal_f16(oracle, M * K, 81, 1.0 / 64)
+    b16, _ = _seeded_normal_f16(oracle, K * N, 82, 1.0 / 64)
+    c = oracle.normal(M * N, 83).reshape(M, N)
+    a_h = torch.from_numpy(a16.view(np.int16)).view(torch.float16).reshape(M, K).pin_memory()
+    b_h = torch.from_numpy(b16.view(np.int16)).view(torch.float16).reshape(K, N).pin_memory()
+    c_h = torch.from_numpy(c.copy()).pin_memory()
+    a_d = torch.empty(M, K, dtype=torch.float16, device=dev)
+    b_d = torch.empty(K, N, dtype=torch.float16, device=dev)
+    c_d = torch.empty(M, N, dtype=torch.float32, device=dev)
+    kernels.gemm_host(a_h, b_h, c_h, a_d, b_d, c_d)
+    torch.cuda.synchronize()
+    a2, b2, c2 = a_h.to(dev), b_h.to(dev), torch.from_numpy(c).to(dev)
+    kernels.gemm(a2, b2, c2)
+    torch.cuda.synchronize()
+    got, ref = c_h.to(dev), c2
+    rel = ((got - ref).norm() / ref.norm()).item()
+    assert rel <= 1e-6, rel
