@@ -138,7 +138,9 @@ int cudair_ctx_synchronize(void);
  * C = A.B + C for n x n row-major matrices: fp16 A and B, fp32 C updated in
  * place, fp32 accumulation.  Same operands as MatMul16 (hopper.go:201); this
  * launcher runs the sm_100a tcgen05/TMA kernel on a persistent grid instead
- * of the reference's one-warp-per-16x16-tile launch.  n must be a multiple of
+ * of the reference's one-warp-per-16x16-tile launch when n > 384; for
+ * n <= 384 it launches that warp-per-tile kernel itself, whose latency is the
+ * lower one there (n = 256: 5.0 against 7.5 us).  n must be a multiple of
  * 16 (the reference's own requirement) and the pointers 16-byte aligned.
  * Asynchronous on stream.
  */
@@ -266,14 +268,15 @@ int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c,
 
 /*
  * out[i] = a[i] + b[i] for i < n (fp32, round-to-nearest: bit-exact with a
- * CPU add).  Same operands as VecAdd (vecadd.go:6); the launcher sizes a
- * persistent grid over the SMs.  Any alignment is accepted.  Asynchronous.
+ * CPU add).  Same operands as VecAdd (vecadd.go:6); the launcher runs one
+ * block per chunk of 512 16-byte vectors, so the hardware hands chunks to SMs
+ * as they finish.  Any alignment is accepted.  Asynchronous.
  */
 int cudair_vecadd(const float *a, const float *b, float *out, int32_t n, void *stream);
 
 /*
- * The rest of the vecadd package (vecadd.go:13-28), streamed like VecAdd on
- * a persistent grid: y[i] = alpha * x[i] + y[i] (product and sum rounded
+ * The rest of the vecadd package (vecadd.go:13-28), streamed like VecAdd in
+ * chunks: y[i] = alpha * x[i] + y[i] (product and sum rounded
  * separately, as the reference's check computes them) and x[i] = x[i] * x[i]
  * in place.  Any alignment.  Asynchronous.
  */

@@ -1,6 +1,6 @@
 """The streaming kernels at the largest length their int32 `n` allows
 (VecAdd, Saxpy and Square at 2^31 - 1 elements, 8 GiB per vector; ReduceF32
-at the largest multiple of 32): no 32-bit index overflows in the grid-stride
+at the largest multiple of 32): no 32-bit index overflows in the chunk
 loops, the vector body or the scalar tail.  Operands are closed-form (small
 integers and halves, exact in fp32), generated and checked on the GPU in
 chunks, so nothing of the 8 GiB vectors crosses the host link."""
