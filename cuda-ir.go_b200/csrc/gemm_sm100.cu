@@ -767,9 +767,11 @@ int device_info(DeviceInfo **out) {
         cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
         cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
     }
-    if (d.major != 10)
+    // sm_100a code (tcgen05, the arch-specific features) runs on compute
+    // capability 10.0 only, not on later 10.x parts.
+    if (d.major != 10 || d.minor != 0)
         return set_error(CUDAIR_ERR_UNSUPPORTED,
-                         "cudair: device %d has compute capability %d.%d; this build targets sm_100a",
+                         "cudair: device %d has compute capability %d.%d; this build targets sm_100a (10.0)",
                          dev, d.major, d.minor);
     if (!d.attr_set) {
         const struct {

@@ -17,6 +17,9 @@ constexpr int kStreamThreads = 512;
 // 512 x V 16-byte vectors per block (V = vectors per thread: 1 for VecAdd and
 // Saxpy, 2 for Square), as many blocks as chunks.
 int stream_grid(int32_t n, int vectors_per_thread, unsigned *blocks_out) {
+    int sms = 0;
+    int rc = sm_count_current_device(&sms);  // refuses a device other than sm_100
+    if (rc != CUDAIR_OK) return rc;
     const int64_t vec_work = (static_cast<int64_t>(n) + 3) / 4;
     const int64_t chunk = static_cast<int64_t>(kStreamThreads) * vectors_per_thread;
     int64_t blocks = (vec_work + chunk - 1) / chunk;
@@ -87,7 +90,7 @@ CUDAIR_API int cudair_reduce_f32(const float *in, float *out, int32_t n, void *s
     if (n == 0) return CUDAIR_OK;
     if (!in || !out) return set_error(CUDAIR_ERR_INVALID, "cudair: ReduceF32: nil pointer");
     int sms = 0;
-    int rc = sm_count_current_device(&sms);
+    int rc = sm_count_current_device(&sms);  // also refuses a device other than sm_100
     if (rc != CUDAIR_OK) return rc;
     // The kernel reads one element per launched thread, so the launch covers
     // exactly n threads: 256-thread blocks when they divide n, else warps.
