@@ -25,6 +25,11 @@ def _need(t, dtype, name):
         raise CudairError(1, f"cudair: {name} must be a CUDA tensor")
     if t.dtype != dtype:
         raise CudairError(1, f"cudair: {name} must be {dtype}, got {t.dtype}")
+    # The library launches on the current device; a tensor of another GPU
+    # would be read across NVLink by the kernels (or fail to launch).
+    cur = torch.cuda.current_device()
+    if t.device.index != cur:
+        raise CudairError(1, f"cudair: {name} is on {t.device}, the current device is cuda:{cur}")
 
 
 def matmul16(a, b, c, stream=None) -> None:

@@ -90,3 +90,20 @@ def test_row_sharded_gemm_two_gpus(dev):
     for r in range(world):
         assert res[r]["b_ok"], f"rank {r}: B differs from rank 0's after the peer copy"
         assert res[r]["rel"] <= 1e-3 and res[r]["max"] <= res[r]["bound"], res[r]
+
+
+def test_tensor_on_another_gpu_is_refused(dev):
+    # The launchers run on the current device; a tensor of another GPU is
+    # refused before anything is launched (its kernels would otherwise read it
+    # across NVLink).
+    import torch
+    from cudair import kernels
+    from cudair._lib import CudairError
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with torch.cuda.device(0):
+        a = torch.ones(1024, device="cuda:1")
+        b = torch.ones(1024, device="cuda:0")
+        out = torch.empty(1024, device="cuda:0")
+        with pytest.raises(CudairError, match="current device is cuda:0"):
+            kernels.vecadd(a, b, out)
