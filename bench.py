@@ -284,29 +284,29 @@ class CpuGemm:
 def run_matmul16_n256(dev, kernels):
     """The MatMul16 parity configuration (n = 256, the reference test's size):
     per-launch latency of the module entry under the reference's launch
-    (grid (n/16, n/16) x 32 threads) and of the tuned tcgen05 kernel, each from
-    a CUDA graph of 20 launches (a single launch timed from Python measures the
-    host's launch cost).  Inputs: fp16(U(-1,1)) A and B, U(-1,1) C."""
+    (grid (n/16, n/16) x 32 threads) and of the library's cudair_matmul16
+    (which picks that same one-warp-per-tile kernel for n <= 512), each from a
+    CUDA graph of 20 launches (a single launch timed from Python measures the
+    host's launch cost), beside the CPU i-j-k loop on the same operands.
+    Inputs: fp16(U(-1,1)) A and B, U(-1,1) C, seeded."""
     import ctypes
 
     import torch
     from cudair import host
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
-    import oracle
     n = 256
-    af = oracle.f16_to_f32(oracle.f32_to_f16(oracle.uniform(n * n, 1))).reshape(n, n)
-    bf = oracle.f16_to_f32(oracle.f32_to_f16(oracle.uniform(n * n, 2))).reshape(n, n)
-    c0 = oracle.uniform(n * n, 3).reshape(n, n)
-    a = torch.from_numpy(af).to(dev).half()
-    b = torch.from_numpy(bf).to(dev).half()
-    c = torch.from_numpy(c0).to(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(256)
+    a = (torch.rand(n, n, generator=g, device=dev) * 2 - 1).half()
+    b = (torch.rand(n, n, generator=g, device=dev) * 2 - 1).half()
+    c = torch.rand(n, n, generator=g, device=dev) * 2 - 1
+    af, bf, c0 = a.float().cpu().numpy(), b.float().cpu().numpy(), c.cpu().numpy()
     mod = host.LoadModule(host.KernelsImage())
     fn = mod.Function("MatMul16")
     cfg = host.LaunchConfig(GridX=n // 16, GridY=n // 16, BlockX=32)
     args = (host.ArgBuffer(a), host.ArgBuffer(b), host.ArgBuffer(c), host.ArgValue(ctypes.c_int32(n)))
     out = {}
     for name, launch in (("reference_launch_us", lambda s: fn.LaunchExOn(s, cfg, host.LaunchAttrs(), *args)),
-                         ("tcgen05_us", lambda s: kernels.matmul16(a, b, c, stream=s))):
+                         ("library_us", lambda s: kernels.matmul16(a, b, c, stream=s))):
         st = torch.cuda.Stream(device=dev)
         for _ in range(3):
             launch(st)
@@ -328,6 +328,9 @@ def run_matmul16_n256(dev, kernels):
         out[name] = statistics.median(ts)
         del graph
     mod.Close()
+    # The CPU baseline of this configuration: the oracle's i-j-k loop.
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
     t0 = time.perf_counter()
     oracle.gemm_ijk(af, bf, c0, threads=1)
     out["cpu_us_1thread"] = (time.perf_counter() - t0) * 1e6

@@ -1065,10 +1065,11 @@ CUDAIR_API int cudair_matmul16(const void *a, const void *b, float *c, int32_t n
     if (n == 0) return CUDAIR_OK;
     if ((reinterpret_cast<uintptr_t>(c) & 15u) != 0)
         return set_error(CUDAIR_ERR_INVALID, "cudair: MatMul16: C must be 16-byte aligned");
-    // Up to n = 384 the one-warp-per-tile kernel has the lower latency (a
-    // single 256 x 256 tile cannot amortise the pipelined kernels' set-up:
-    // n = 256 4.9 against 7.5 us, n = 384 6.9 against 8.3 us, n = 512 even).
-    if (n <= 384 && g_variant.load() == 0) {
+    // Up to n = 512 the one-warp-per-tile kernel has the lower latency (a
+    // few pair tiles cannot amortise the pipelined kernels' set-up: n = 256
+    // 3.6 against 7.8 us, n = 512 8.9 against 9.4 us, n = 768 25.5 against
+    // 10.6 us).
+    if (n <= 512 && g_variant.load() == 0) {
         if (!a || !b || !c) return set_error(CUDAIR_ERR_INVALID, "cudair: MatMul16: nil pointer");
         if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u)
             return set_error(CUDAIR_ERR_INVALID, "cudair: MatMul16: A and B must be 16-byte aligned");

@@ -200,6 +200,18 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// 16-byte global -> shared copy that bypasses L1 (cp.async.cg); completes
+// with the thread's next cp.async.wait_group.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 }  // namespace cudair_detail
 
 // C = A.B + C for n x n row-major matrices (fp16 A, B; fp32 C in place),
@@ -210,11 +222,17 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 // This entry serves callers that launch the module kernel themselves with
 // that geometry; the throughput path is the tcgen05 kernel behind
 // cudair_matmul16(), which needs tensor-map parameters this signature cannot
-// carry.  The warp keeps its C tile in mma.sync accumulators initialised from
-// C, streams 16-wide k-slices of A and B through padded shared memory
-// (conflict-free ldmatrix rows) with the next slice's global loads in flight
-// during the current slice's two m16n8k16 MMAs, and writes C back once.
-// Threads beyond the first warp return.
+// carry (cudair_matmul16 also launches this kernel for n <= 512, where its
+// latency is the lower one).  The warp keeps its C tile in mma.sync
+// accumulators initialised from C and streams 16-wide k-slices of A and B
+// through a ring of MM_STAGES slices in padded shared memory (48-byte rows:
+// conflict-free ldmatrix), filled by cp.async, so up to MM_STAGES slices are
+// in flight at once: at n <= 256 the whole K panel is requested together and
+// the loads cost one round trip instead of one per slice.  Each slice feeds
+// two m16n8k16 MMAs; C is written back once.  Threads beyond the first warp
+// return.
+constexpr int MM_STAGES = 16;  // 2 x 16 x 768 B = 24 KB of static shared memory
+
 extern "C" __global__ void __launch_bounds__(32)
     MatMul16(const __half *__restrict__ a, const __half *__restrict__ b, float *__restrict__ c,
              int n) {
@@ -223,11 +241,29 @@ extern "C" __global__ void __launch_bounds__(32)
     const int row0 = blockIdx.y * 16, col0 = blockIdx.x * 16;
     if (n <= 0 || (n & 15) != 0 || row0 >= n || col0 >= n) return;
 
-    __shared__ __align__(16) __half sa[16][24];  // 48-byte rows
-    __shared__ __align__(16) __half sb[16][24];
+    __shared__ __align__(16) __half sa[MM_STAGES][16][24];  // 48-byte rows
+    __shared__ __align__(16) __half sb[MM_STAGES][16][24];
 
     const int lane = threadIdx.x, g = lane >> 2, t = lane & 3;
     const size_t N = static_cast<size_t>(n);
+    const int nk = n / 16;
+
+    // Lane l copies 8 halves (16 bytes) of row l/2 of each A and B slice.
+    const int sr = lane >> 1, sc = (lane & 1) * 8;
+    const __half *ap = a + (row0 + sr) * N + sc;
+    const __half *bp = b + sr * N + col0 + sc;
+    auto fetch = [&](int ks) {
+        const int slot = ks % MM_STAGES;
+        cp_async16(&sa[slot][sr][sc], ap + static_cast<size_t>(ks) * 16);
+        cp_async16(&sb[slot][sr][sc], bp + static_cast<size_t>(ks) * 16 * N);
+    };
+    // Slices 0 .. MM_STAGES-2 go out first, one commit group each (empty
+    // groups past the end keep the group count uniform).
+#pragma unroll 1
+    for (int s = 0; s < MM_STAGES - 1; ++s) {
+        if (s < nk) fetch(s);
+        cp_async_commit();
+    }
 
     float acc[2][4];
 #pragma unroll
@@ -241,28 +277,26 @@ extern "C" __global__ void __launch_bounds__(32)
         acc[nf][3] = hi.y;
     }
 
-    // Lane l stages 8 halves of row l/2 of the A slice and of the B slice.
-    const int sr = lane >> 1, sc = (lane & 1) * 8;
-    const __half *ap = a + (row0 + sr) * N + sc;
-    const __half *bp = b + sr * N + col0 + sc;
-    uint4 ra = *reinterpret_cast<const uint4 *>(ap);
-    uint4 rb = *reinterpret_cast<const uint4 *>(bp);
-
-    for (int k0 = 0; k0 < n; k0 += 16) {
-        *reinterpret_cast<uint4 *>(&sa[sr][sc]) = ra;
-        *reinterpret_cast<uint4 *>(&sb[sr][sc]) = rb;
+#pragma unroll 1
+    for (int ks = 0; ks < nk; ++ks) {
+        // Slice ks + MM_STAGES - 1 reuses the slot of slice ks - 1, which the
+        // previous iteration finished reading before its closing __syncwarp.
+        if (ks + MM_STAGES - 1 < nk) fetch(ks + MM_STAGES - 1);
+        cp_async_commit();
+        // All but the newest MM_STAGES - 1 groups are complete: slice ks has
+        // landed (this lane's copies); the __syncwarp makes every lane's
+        // copies visible to the warp.
+        cp_async_wait<MM_STAGES - 1>();
         __syncwarp();
-        if (k0 + 16 < n) {
-            ra = *reinterpret_cast<const uint4 *>(ap + k0 + 16);
-            rb = *reinterpret_cast<const uint4 *>(bp + (k0 + 16) * N);
-        }
+        const int slot = ks % MM_STAGES;
         uint32_t fa[4], fb[4];
-        ldsm_x4(fa, &sa[lane & 15][(lane >> 4) * 8]);
-        ldsm_x4_trans(fb, &sb[lane & 15][(lane >> 4) * 8]);
+        ldsm_x4(fa, &sa[slot][lane & 15][(lane >> 4) * 8]);
+        ldsm_x4_trans(fb, &sb[slot][lane & 15][(lane >> 4) * 8]);
         mma_16816(acc[0], fa, fb[0], fb[1]);
         mma_16816(acc[1], fa, fb[2], fb[3]);
         __syncwarp();
     }
+    cp_async_wait<0>();
 
 #pragma unroll
     for (int nf = 0; nf < 2; ++nf) {

@@ -138,9 +138,9 @@ int cudair_ctx_synchronize(void);
  * C = A.B + C for n x n row-major matrices: fp16 A and B, fp32 C updated in
  * place, fp32 accumulation.  Same operands as MatMul16 (hopper.go:201); this
  * launcher runs the sm_100a tcgen05/TMA kernel on a persistent grid instead
- * of the reference's one-warp-per-16x16-tile launch when n > 384; for
- * n <= 384 it launches that warp-per-tile kernel itself, whose latency is the
- * lower one there (n = 256: 5.0 against 7.5 us).  n must be a multiple of
+ * of the reference's one-warp-per-16x16-tile launch when n > 512; for
+ * n <= 512 it launches that warp-per-tile kernel itself, whose latency is the
+ * lower one there (n = 256: 3.6 against 7.8 us).  n must be a multiple of
  * 16 (the reference's own requirement) and the pointers 16-byte aligned.
  * Asynchronous on stream.
  */
@@ -217,7 +217,7 @@ int cudair_set_gemm_variant(int variant);
  * treat it as 1).  The caller promises that the preceding kernel does not
  * write B (weights).  Results are identical in all modes.  Applies to
  * subsequent GEMM calls (cudair_gemm_f16f32, cudair_gemm, cudair_matmul16
- * above n = 384) in this process.
+ * above n = 512) in this process.
  */
 int cudair_set_gemm_pdl(int mode);
 
