@@ -159,6 +159,42 @@ def test_vecadd_and_reduce_validation(cudair):
     assert "multiple of 32" in cudair.last_error()
 
 
+def test_saxpy_and_square_validation(cudair):
+    L = cudair.lib()
+    assert L.cudair_saxpy(2.0, None, None, -1, None) == 1
+    assert "Saxpy: n = -1" in cudair.last_error()
+    assert L.cudair_saxpy(2.0, None, None, 0, None) == 0
+    assert L.cudair_saxpy(2.0, None, None, 16, None) == 1
+    assert "Saxpy: nil pointer" in cudair.last_error()
+    assert L.cudair_square(None, -1, None) == 1
+    assert "Square: n = -1" in cudair.last_error()
+    assert L.cudair_square(None, 0, None) == 0
+    assert L.cudair_square(None, 16, None) == 1
+    assert "Square: nil pointer" in cudair.last_error()
+
+
+# The no-alloc few-row entry checks its arguments before it touches the
+# device: sizes beyond its fixed scratch array, pitches and alignment.
+@pytest.mark.parametrize("M,N,K,lda,ldb,ldc,ptr,needle", [
+    (-1, 16, 16, 16, 16, 16, 256, "negative size"),
+    (65, 16, 16, 16, 16, 16, 256, "exceeds the maximum of 64 rows"),
+    (16, 4096 * 128 + 8, 16, 16, 4096 * 128 + 8, 4096 * 128 + 8, 256, "columns"),
+    (16, 16, 16, 8, 16, 16, 256, "too small"),
+    (16, 16, 12, 12, 16, 16, 256, "multiples of 8"),
+    (16, 16, 16, 16, 16, 16, 264, "16-byte aligned"),
+    (16, 16, 16, 16, 16, 16, 0, "nil pointer"),
+])
+def test_noalloc_validation(cudair, M, N, K, lda, ldb, ldc, ptr, needle):
+    rc = cudair.lib().cudair_gemm_f16f32_noalloc(ptr, ptr, ptr, M, N, K, lda, ldb, ldc, None)
+    assert rc == 1 and needle in cudair.last_error(), cudair.last_error()
+
+
+def test_noalloc_empty_sizes_are_noops(cudair):
+    L = cudair.lib()
+    for M, N, K in ((0, 16, 16), (16, 0, 16), (16, 16, 0)):
+        assert L.cudair_gemm_f16f32_noalloc(None, None, None, M, N, K, 16, 16, 16, None) == 0
+
+
 def test_errors_are_thread_local(cudair):
     import threading
     L = cudair.lib()
