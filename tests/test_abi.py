@@ -16,6 +16,46 @@ def test_library_exports_every_header_function(cudair):
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
 
 
+# The ctypes table the Python wrapper binds must match the C declarations in
+# include/cudair_b200.h parameter by parameter: pointer or scalar, and for a
+# scalar its width and signedness.
+_C_SCALARS = {"int": (4, "i"), "int32_t": (4, "i"), "int64_t": (8, "i"), "uint32_t": (4, "u"),
+              "uint64_t": (8, "u"), "size_t": (8, "u"), "float": (4, "f")}
+_C_HANDLES = {"cudair_module", "cudair_function"}  # typedef'd struct pointers
+
+
+def _c_kind(decl):
+    decl = decl.strip()
+    if "*" in decl or "[" in decl:
+        return "ptr"
+    typ = decl.replace("const ", "").split()[0]
+    return "ptr" if typ in _C_HANDLES else _C_SCALARS[typ]
+
+
+def _ctypes_kind(ct):
+    if ct in (ctypes.c_void_p, ctypes.c_char_p) or issubclass(ct, ctypes._Pointer):
+        return "ptr"
+    if ct is ctypes.c_float:
+        return (4, "f")
+    return (ctypes.sizeof(ct), "i" if ct(-1).value < 0 else "u")
+
+
+def test_ctypes_signatures_match_the_header(cudair):
+    import re
+    from cudair import _lib
+    text = re.sub(r"/\*.*?\*/", "", open(_lib.HEADER_PATH).read(), flags=re.S)
+    decls = {m.group(2): (m.group(1).strip(), m.group(3))
+             for m in re.finditer(r"([A-Za-z_][\w \t\*]*?)\b(cudair_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text)}
+    assert set(decls) == set(_lib.SIGNATURES), set(decls) ^ set(_lib.SIGNATURES)
+    for name, (ret, params) in decls.items():
+        restype, argtypes = _lib.SIGNATURES[name]
+        assert (ret == "int") == (restype is ctypes.c_int), name
+        cparams = [] if params.strip() == "void" else [p for p in params.split(",")]
+        assert len(cparams) == len(argtypes), (name, len(cparams), len(argtypes))
+        for i, (cp, ct) in enumerate(zip(cparams, argtypes)):
+            assert _c_kind(cp) == _ctypes_kind(ct), (name, i, cp, ct)
+
+
 def test_module_image_has_reference_entry_points(cudair):
     from cudair import host
     img = host.KernelsImage()
