@@ -9,7 +9,6 @@ beyond the array's limits are refused.
 
 This file is collected last so that a failure here never hides another test.
 """
-import ctypes
 
 import numpy as np
 import pytest
