@@ -149,3 +149,27 @@ def test_generator_pinned(oracle, golden_dir, seed):
 def test_generator_offsets_compose(oracle):
     full = oracle.uniform(1000, 9)
     assert np.array_equal(full[300:700], oracle.uniform(400, 9, offset=300))
+
+
+def test_golden_fixtures_are_reproducible(tmp_path, golden_dir):
+    # tests/golden/make_golden.py (numpy only) regenerates every committed
+    # fixture bit for bit.
+    import json
+    import os
+    import shutil
+    import subprocess
+    import sys
+    shutil.copy(os.path.join(golden_dir, "make_golden.py"), tmp_path)
+    subprocess.run([sys.executable, str(tmp_path / "make_golden.py")], check=True, capture_output=True,
+                   timeout=300)
+    fixtures = [f for f in os.listdir(golden_dir) if f.endswith((".npz", ".json"))]
+    assert fixtures
+    for f in fixtures:
+        a, b = os.path.join(golden_dir, f), str(tmp_path / f)
+        if f.endswith(".npz"):
+            A, B = np.load(a), np.load(b)
+            assert set(A.files) == set(B.files), f
+            for k in A.files:
+                assert np.array_equal(A[k], B[k]), (f, k)
+        else:
+            assert json.load(open(a)) == json.load(open(b)), f
