@@ -48,6 +48,8 @@ SIGNATURES = {
     "cudair_saxpy": (c_int, [ctypes.c_float, c_vp, c_vp, ctypes.c_int32, c_vp]),
     "cudair_square": (c_int, [c_vp, ctypes.c_int32, c_vp]),
     "cudair_reduce_f32": (c_int, [c_vp, c_vp, ctypes.c_int32, c_vp]),
+    "cudair_fill": (c_int, [c_vp, c_u32, c_u32, c_i64, c_u64, c_i64, ctypes.c_double, ctypes.c_double,
+                            c_vp]),
     "cudair_wait_status": (c_int, [_u32p, c_int]),
     "cudair_wait_timeout_selftest": (c_int, [c_u64, c_vp]),
     "cudair_ipc_export": (c_int, [c_vp, c_vp, _u64p]),

@@ -176,6 +176,33 @@ def reduce_f32(x, out, stream=None) -> None:
     check(lib().cudair_reduce_f32(x.data_ptr(), out.data_ptr(), x.numel(), _stream(stream)))
 
 
+FILL_F32, FILL_F16 = 0, 1
+FILL_UNIFORM, FILL_NORMAL = 0, 1
+
+
+def _fill(t, dist, seed, p0, p1, offset, stream):
+    import torch
+    if t.dtype not in (torch.float32, torch.float16):
+        raise CudairError(1, f"cudair: fill: tensor must be float32 or float16, got {t.dtype}")
+    _need(t, t.dtype, "out")
+    if not t.is_contiguous():
+        raise CudairError(1, "cudair: fill: tensor must be contiguous")
+    check(lib().cudair_fill(t.data_ptr(), FILL_F16 if t.dtype == torch.float16 else FILL_F32, dist,
+                            t.numel(), seed, offset, float(p0), float(p1), _stream(stream)))
+
+
+def fill_uniform(t, seed: int, lo=-1.0, hi=1.0, offset: int = 0, stream=None) -> None:
+    """Fills t (contiguous fp32 or fp16) with elements offset.. of the seeded
+    U(lo, hi) stream (cudair_fill), bit for bit the CPU oracle's values."""
+    _fill(t, FILL_UNIFORM, seed, lo, hi, offset, stream)
+
+
+def fill_normal(t, seed: int, mean=0.0, std=1.0, offset: int = 0, stream=None) -> None:
+    """Fills t (contiguous fp32 or fp16) with elements offset.. of the seeded
+    N(mean, std) stream (cudair_fill), bit for bit the CPU oracle's values."""
+    _fill(t, FILL_NORMAL, seed, mean, std, offset, stream)
+
+
 def wait_status(clear: bool = True) -> int:
     """Synchronises and returns the bounded-wait status word (0 = no wait gave
     up); raises CudairError(ERR_TIMEOUT) when a bit is set."""

@@ -289,6 +289,30 @@ int cudair_square(float *x, int32_t n, void *stream);
  */
 int cudair_reduce_f32(const float *in, float *out, int32_t n, void *stream);
 
+/* ---- seeded synthetic operands -------------------------------------------- */
+
+enum { CUDAIR_FILL_F32 = 0, CUDAIR_FILL_F16 = 1 };
+enum { CUDAIR_FILL_UNIFORM = 0, CUDAIR_FILL_NORMAL = 1 };
+
+/*
+ * Writes elements offset .. offset + n - 1 of the seeded stream `seed` to
+ * out (n contiguous fp32 or fp16 values, out_type CUDAIR_FILL_F32 / _F16):
+ * element i comes from the word splitmix64(seed * 0x9E3779B97F4A7C15 + i)
+ * alone, as
+ *   CUDAIR_FILL_UNIFORM  U(p0, p1): p0 + (p1 - p0) * (w >> 40) * 2^-24 in fp32
+ *   CUDAIR_FILL_NORMAL   N(p0, p1): Box-Muller on two 24-bit uniforms of w
+ *                        in double, rounded to fp32
+ * and, for fp16, the fp32 value rounded to nearest even.  Every step is a
+ * correctly rounded IEEE operation in a fixed order (the logarithm and
+ * cosine by short series), so the values are bit for bit those of the CPU
+ * restatement of the same steps.  No counterpart in the reference, whose
+ * tests build their inputs on the host: this generates the benchmark's and
+ * the tests' seeded operands where they live, a rank's slice of a matrix
+ * included (offset = its first element).  Asynchronous on stream.
+ */
+int cudair_fill(void *out, uint32_t out_type, uint32_t dist, int64_t n, uint64_t seed,
+                int64_t offset, double p0, double p1, void *stream);
+
 /* ---- failure detection ----------------------------------------------------- */
 
 /*

@@ -418,18 +418,103 @@ EXPORT void oracle_fill_uniform(float *out, int64_t n, uint64_t seed,
 }
 
 /*
+ * The logarithm and cosine of the Box-Muller transform below, written with
+ * correctly rounded double +, -, *, / and sqrt only, in a fixed order, so
+ * that any IEEE-754 evaluation of the same steps (numpy in
+ * tests/golden/make_golden.py, the library's device fill kernel) gets the
+ * same bits; libm's log and cos differ between implementations in the last
+ * bit.  The coefficients are exact hex literals of the rounded reciprocals.
+ *
+ * ln(m 2^-24), integer 1 <= m <= 2^24: m = f 2^e with f in [sqrt(1/2),
+ * sqrt(2)); ln f = 2 atanh(s), s = (f-1)/(f+1), by the series
+ * atanh(s) = s (1 + s^2/3 + s^4/5 + ...) to the s^24 term (|s| <= 0.1716,
+ * so the first dropped term is below 2^-60 of the sum).
+ */
+static const double kLnCoef[13] = {
+    0x1.0000000000000p+0, 0x1.5555555555555p-2, 0x1.999999999999ap-3, 0x1.2492492492492p-3,
+    0x1.c71c71c71c71cp-4, 0x1.745d1745d1746p-4, 0x1.3b13b13b13b14p-4, 0x1.1111111111111p-4,
+    0x1.e1e1e1e1e1e1ep-5, 0x1.af286bca1af28p-5, 0x1.8618618618618p-5, 0x1.642c8590b2164p-5,
+    0x1.47ae147ae147bp-5}; /* 1/(2k+1) */
+/* Taylor series of sin and cos in nested form: 1/((2k)(2k+1)), 1/((2k-1)(2k)). */
+static const double kSinCoef[11] = {
+    0.0, 0x1.5555555555555p-3, 0x1.999999999999ap-5, 0x1.8618618618618p-6, 0x1.c71c71c71c71cp-7,
+    0x1.29e4129e4129ep-7, 0x1.a41a41a41a41ap-8, 0x1.3813813813814p-8, 0x1.e1e1e1e1e1e1ep-9,
+    0x1.7f405fd017f40p-9, 0x1.3813813813814p-9};
+static const double kCosCoef[11] = {
+    0.0, 0x1.0000000000000p-1, 0x1.5555555555555p-4, 0x1.1111111111111p-5, 0x1.2492492492492p-6,
+    0x1.6c16c16c16c17p-7, 0x1.f07c1f07c1f08p-8, 0x1.6816816816817p-8, 0x1.1111111111111p-8,
+    0x1.ac5701ac5701bp-9, 0x1.58ed2308158edp-9};
+static const double kLn2 = 0x1.62e42fefa39efp-1;
+static const double kSqrt2 = 0x1.6a09e667f3bcdp+0;
+static const double kPiOver2p23 = 0x1.921fb54442d18p-22; /* pi / 2^23 */
+
+static double ln_u24(uint32_t m)
+{
+    int e = 31 - __builtin_clz(m);           /* floor(log2 m) */
+    double f = (double)m / (double)(1u << e); /* exact, in [1, 2) */
+    if (f > kSqrt2) {
+        f = f * 0.5; /* exact */
+        e += 1;
+    }
+    double s = (f - 1.0) / (f + 1.0); /* f - 1 and f + 1 are exact */
+    double w = s * s;
+    double p = kLnCoef[12];
+    for (int k = 11; k >= 0; k--)
+        p = kLnCoef[k] + w * p;
+    double t = (2.0 * s) * p;
+    return t + (double)(e - 24) * kLn2;
+}
+
+/* cos(2 pi v 2^-24), integer 0 <= v < 2^24: the quadrant q and the angle
+ * x = r pi 2^-23 inside it (r < 2^22) come from the integer exactly; for
+ * x > pi/4 the complement pi/2 - x = (2^22 - r) pi 2^-23 is used, so the
+ * series (to the x^20 term) only sees |x| <= pi/4. */
+static double cos_2pi_u24(uint32_t v)
+{
+    uint32_t q = v >> 22, r = v & 0x3fffffu;
+    int want_sin = (int)(q & 1u);      /* q = 1, 3: -sin x, sin x */
+    int neg = (q == 1u || q == 2u);
+    uint32_t y = r;
+    if (r > (1u << 21)) {
+        y = (1u << 22) - r;
+        want_sin ^= 1;
+    }
+    double x = (double)y * kPiOver2p23;
+    double x2 = x * x;
+    double p = 1.0;
+    double res;
+    if (want_sin) {
+        for (int k = 10; k >= 1; k--)
+            p = 1.0 - (x2 * kSinCoef[k]) * p;
+        res = x * p;
+    } else {
+        for (int k = 10; k >= 1; k--)
+            p = 1.0 - (x2 * kCosCoef[k]) * p;
+        res = p;
+    }
+    return neg ? -res : res;
+}
+
+/*
  * N(mean, std) by Box-Muller on two 24-bit uniforms taken from one 64-bit
  * word: u1 = (bits 40..63 + 1) * 2^-24 in (0,1], u2 = bits 8..31 * 2^-24 in
- * [0,1); z = sqrt(-2 ln u1) cos(2 pi u2), evaluated in double, then rounded.
+ * [0,1); z = sqrt(-2 ln u1) cos(2 pi u2) in double (ln and cos as above),
+ * then mean + std z rounded to float.
  */
+static double normal_z(uint64_t w)
+{
+    uint32_t m = (uint32_t)((w >> 40) & 0xffffffu) + 1u;
+    uint32_t v = (uint32_t)((w >> 8) & 0xffffffu);
+    double r = sqrt(-2.0 * ln_u24(m));
+    return r * cos_2pi_u24(v);
+}
+
 static void normal_range(void *p, int64_t lo, int64_t hi)
 {
     struct fill_ctx *c = (struct fill_ctx *)p;
     for (int64_t i = lo; i < hi; i++) {
         uint64_t w = stream_word(c->seed, (uint64_t)(c->offset + i));
-        double u1 = ((double)((w >> 40) & 0xffffffu) + 1.0) / 16777216.0;
-        double u2 = (double)((w >> 8) & 0xffffffu) / 16777216.0;
-        double z = sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
+        double z = normal_z(w);
         c->out[i] = (float)(c->a + c->b * z);
     }
 }

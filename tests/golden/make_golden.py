@@ -15,7 +15,8 @@ of the C oracle, from the closed-form inputs of cuda-ir.go's own tests:
                        to infinity, which test_oracle.py checks separately).
   generator.json       the first words / values of the seeded streams the
                        tests and the bench use, from a numpy restatement of the
-                       counter-based splitmix64 generator.
+                       counter-based splitmix64 generator, and sha256 pins of
+                       2^16-value runs of the normal streams.
   matmul16_n256.npz    the seeded n=256 MatMul16 case (A,B = fp16(U(-1,1)),
                        C = U(-1,1), seeds 1,2,3): expected C in float64,
                        rounded to float32.
@@ -56,11 +57,68 @@ def uniform(seed: int, n: int, lo=-1.0, hi=1.0) -> np.ndarray:
     return (np.float32(lo) + (np.float32(hi) - np.float32(lo)) * u).astype(np.float32)
 
 
+# Box-Muller with its logarithm and cosine as fixed sequences of correctly
+# rounded float64 operations (numpy never fuses a multiply and an add), the
+# same steps in the same order as the oracle's C code: ln(m 2^-24) through
+# ln f = 2 atanh((f-1)/(f+1)) with f in [sqrt(1/2), sqrt(2)), and cos(2 pi
+# v 2^-24) by quadrant, complement above pi/4 and the nested Taylor series.
+LN_COEF = [float.fromhex(h) for h in (
+    "0x1.0000000000000p+0", "0x1.5555555555555p-2", "0x1.999999999999ap-3", "0x1.2492492492492p-3",
+    "0x1.c71c71c71c71cp-4", "0x1.745d1745d1746p-4", "0x1.3b13b13b13b14p-4", "0x1.1111111111111p-4",
+    "0x1.e1e1e1e1e1e1ep-5", "0x1.af286bca1af28p-5", "0x1.8618618618618p-5", "0x1.642c8590b2164p-5",
+    "0x1.47ae147ae147bp-5")]
+SIN_COEF = [0.0] + [float.fromhex(h) for h in (
+    "0x1.5555555555555p-3", "0x1.999999999999ap-5", "0x1.8618618618618p-6", "0x1.c71c71c71c71cp-7",
+    "0x1.29e4129e4129ep-7", "0x1.a41a41a41a41ap-8", "0x1.3813813813814p-8", "0x1.e1e1e1e1e1e1ep-9",
+    "0x1.7f405fd017f40p-9", "0x1.3813813813814p-9")]
+COS_COEF = [0.0] + [float.fromhex(h) for h in (
+    "0x1.0000000000000p-1", "0x1.5555555555555p-4", "0x1.1111111111111p-5", "0x1.2492492492492p-6",
+    "0x1.6c16c16c16c17p-7", "0x1.f07c1f07c1f08p-8", "0x1.6816816816817p-8", "0x1.1111111111111p-8",
+    "0x1.ac5701ac5701bp-9", "0x1.58ed2308158edp-9")]
+LN2 = float.fromhex("0x1.62e42fefa39efp-1")
+SQRT2 = float.fromhex("0x1.6a09e667f3bcdp+0")
+PI_OVER_2P23 = float.fromhex("0x1.921fb54442d18p-22")
+
+
+def ln_u24(m: np.ndarray) -> np.ndarray:
+    mant, ex = np.frexp(m.astype(np.float64))  # m = mant 2^ex, mant in [0.5, 1)
+    f = mant * 2.0
+    e = (ex - 1).astype(np.float64)
+    big = f > SQRT2
+    f = np.where(big, f * 0.5, f)
+    e = np.where(big, e + 1.0, e)
+    s = (f - 1.0) / (f + 1.0)
+    w = s * s
+    p = np.full_like(s, LN_COEF[12])
+    for k in range(11, -1, -1):
+        p = LN_COEF[k] + w * p
+    return (2.0 * s) * p + (e - 24.0) * LN2
+
+
+def cos_2pi_u24(v: np.ndarray) -> np.ndarray:
+    q = v >> np.uint64(22)
+    r = v & np.uint64(0x3FFFFF)
+    want_sin = (q & np.uint64(1)) == 1
+    neg = (q == 1) | (q == 2)
+    comp = r > (1 << 21)
+    y = np.where(comp, np.uint64(1 << 22) - r, r)
+    want_sin = want_sin ^ comp
+    x = y.astype(np.float64) * PI_OVER_2P23
+    x2 = x * x
+    ps = np.ones_like(x)
+    pc = np.ones_like(x)
+    for k in range(10, 0, -1):
+        ps = 1.0 - (x2 * SIN_COEF[k]) * ps
+        pc = 1.0 - (x2 * COS_COEF[k]) * pc
+    res = np.where(want_sin, x * ps, pc)
+    return np.where(neg, -res, res)
+
+
 def normal(seed: int, n: int, mean=0.0, std=1.0) -> np.ndarray:
     w = stream_words(seed, n)
-    u1 = (((w >> np.uint64(40)) & np.uint64(0xFFFFFF)).astype(np.float64) + 1.0) / 16777216.0
-    u2 = ((w >> np.uint64(8)) & np.uint64(0xFFFFFF)).astype(np.float64) / 16777216.0
-    z = np.sqrt(-2.0 * np.log(u1)) * np.cos(6.283185307179586 * u2)
+    m = ((w >> np.uint64(40)) & np.uint64(0xFFFFFF)) + np.uint64(1)
+    v = (w >> np.uint64(8)) & np.uint64(0xFFFFFF)
+    z = np.sqrt(-2.0 * ln_u24(m)) * cos_2pi_u24(v)
     return (mean + std * z).astype(np.float32)
 
 
@@ -121,6 +179,12 @@ def main():
             "uniform": [float(v) for v in uniform(seed, 8)],
             "normal": [float(v) for v in normal(seed, 8)],
         }
+    # Longer runs of the normal stream, pinned by hash: the bench's operand
+    # scale 1/sqrt(8192) and the unit scale, 2^16 values each.
+    gen["normal_sha256"] = {
+        f"{seed}/{name}": hashlib.sha256(normal(seed, 1 << 16, 0.0, std).tobytes()).hexdigest()
+        for seed in (6, 7, 8, 9, 11, 12)
+        for name, std in (("1", 1.0), ("1/sqrt(8192)", 1.0 / np.sqrt(8192.0)))}
     json.dump(gen, open(os.path.join(HERE, "generator.json"), "w"), indent=1)
 
     # -- seeded n = 256 MatMul16 case

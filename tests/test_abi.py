@@ -20,7 +20,8 @@ def test_library_exports_every_header_function(cudair):
 # include/cudair_b200.h parameter by parameter: pointer or scalar, and for a
 # scalar its width and signedness.
 _C_SCALARS = {"int": (4, "i"), "int32_t": (4, "i"), "int64_t": (8, "i"), "uint32_t": (4, "u"),
-              "uint64_t": (8, "u"), "size_t": (8, "u"), "float": (4, "f")}
+              "uint64_t": (8, "u"), "size_t": (8, "u"), "float": (4, "f"),
+              "double": (8, "f")}
 _C_HANDLES = {"cudair_module", "cudair_function"}  # typedef'd struct pointers
 
 
@@ -37,6 +38,8 @@ def _ctypes_kind(ct):
         return "ptr"
     if ct is ctypes.c_float:
         return (4, "f")
+    if ct is ctypes.c_double:
+        return (8, "f")
     return (ctypes.sizeof(ct), "i" if ct(-1).value < 0 else "u")
 
 
@@ -211,6 +214,22 @@ def test_saxpy_and_square_validation(cudair):
     assert L.cudair_square(None, 0, None) == 0
     assert L.cudair_square(None, 16, None) == 1
     assert "Square: nil pointer" in cudair.last_error()
+
+
+def test_fill_validation(cudair):
+    # Checked before the device is touched.
+    L = cudair.lib()
+    assert L.cudair_fill(None, 2, 0, 4, 1, 0, 0.0, 1.0, None) == 1
+    assert "output type 2" in cudair.last_error()
+    assert L.cudair_fill(None, 0, 5, 4, 1, 0, 0.0, 1.0, None) == 1
+    assert "distribution 5" in cudair.last_error()
+    assert L.cudair_fill(None, 0, 0, -1, 1, 0, 0.0, 1.0, None) == 1
+    assert L.cudair_fill(None, 1, 1, 4, 1, -3, 0.0, 1.0, None) == 1
+    assert L.cudair_fill(None, 0, 0, 0, 1, 0, 0.0, 1.0, None) == 0
+    assert L.cudair_fill(None, 0, 0, 4, 1, 0, 0.0, 1.0, None) == 1
+    assert "nil pointer" in cudair.last_error()
+    assert L.cudair_fill(18, 0, 0, 4, 1, 0, 0.0, 1.0, None) == 1
+    assert "aligned" in cudair.last_error()
 
 
 # The no-alloc few-row entry checks its arguments before it touches the
