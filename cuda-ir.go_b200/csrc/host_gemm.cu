@@ -1,6 +1,8 @@
-// host_gemm.cu - C = A.B + C from host buffers, the flow of the reference's
-// MatMul16 test (advanced_test.go:466-483: copy A, B and C to the device,
-// launch, copy C back) as one call whose copies overlap the GEMM.
+// host_gemm.cu - the entry points that take host buffers: the flows of the
+// reference's tests (copy the inputs to the device, launch, copy the result
+// back) as single calls whose copies overlap the kernels.  GEMM first:
+// C = A.B + C as in the MatMul16 test (advanced_test.go:466-483); VecAdd
+// (main_test.go:31-48) and the square MatMul16 call follow at the end.
 //
 // C is cut into tiles of rows x columns.  Three streams carry the work:
 //   in       H2D, in order: for each column block j, the columns of B it
@@ -191,5 +193,98 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
     }
     CUDAIR_TRY(cudaStreamWaitEvent(s, p->block_out[t - 1], 0), "cudaStreamWaitEvent");
 #undef CUDAIR_TRY
+    return CUDAIR_OK;
+}
+
+// =============================================================================
+// VecAdd from host buffers: the flow of the reference's TestVecAdd
+// (main_test.go:31-48: upload a and b, launch VecAdd, copy out back) as one
+// call.  The vectors are cut into chunks; chunk i+1 is copied in on the
+// in-stream while chunk i is added on the caller's stream and chunk i-1 is
+// copied out on the out-stream.
+// =============================================================================
+CUDAIR_API int cudair_vecadd_host(const float *a_host, const float *b_host, float *out_host, int32_t n,
+                                  float *a_dev, float *b_dev, float *out_dev, int32_t chunk,
+                                  void *stream) {
+    clear_error();
+    if (n < 0 || chunk < 0)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: vecadd_host: n = %d, chunk = %d", n, chunk);
+    if (n == 0) return CUDAIR_OK;
+    if (!a_host || !b_host || !out_host || !a_dev || !b_dev || !out_dev)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: vecadd_host: nil pointer");
+    // By default about sixteen chunks of at least 2^20 elements; a chunk is
+    // a multiple of 4 elements, so every chunk keeps the buffers' 16-byte
+    // alignment; at most kMaxBlocks chunks.
+    int64_t ch = chunk;
+    if (ch == 0) ch = ((static_cast<int64_t>(n) + 15) / 16 < (1 << 20)) ? (1 << 20) : (static_cast<int64_t>(n) + 15) / 16;
+    ch = (ch + 3) / 4 * 4;
+    if ((n + ch - 1) / ch > kMaxBlocks) ch = ((n + kMaxBlocks - 1) / kMaxBlocks + 3) / 4 * 4;
+    const int chunks = static_cast<int>((n + ch - 1) / ch);
+
+    int rc = ensure_context();
+    if (rc != CUDAIR_OK) return rc;
+    std::lock_guard<std::mutex> lk(g_pipe_mu);
+    HostPipe *p = nullptr;
+    if ((rc = pipe_for_current_device(&p)) != CUDAIR_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+#define CUDAIR_TRY(call, what)                                       \
+    do {                                                             \
+        if ((e = (call)) != cudaSuccess) return cuda_error(e, what); \
+    } while (0)
+    CUDAIR_TRY(cudaEventRecord(p->start, s), "cudaEventRecord");
+    CUDAIR_TRY(cudaStreamWaitEvent(p->in, p->start, 0), "cudaStreamWaitEvent");
+    CUDAIR_TRY(cudaStreamWaitEvent(p->out, p->start, 0), "cudaStreamWaitEvent");
+    for (int i = 0; i < chunks; ++i) {
+        const int64_t i0 = i * ch, len = (n - i0 < ch) ? n - i0 : ch;
+        const size_t bytes = static_cast<size_t>(len) * 4;
+        CUDAIR_TRY(cudaMemcpyAsync(a_dev + i0, a_host + i0, bytes, cudaMemcpyHostToDevice, p->in), "H2D of a");
+        CUDAIR_TRY(cudaMemcpyAsync(b_dev + i0, b_host + i0, bytes, cudaMemcpyHostToDevice, p->in), "H2D of b");
+        CUDAIR_TRY(cudaEventRecord(p->block_in[i], p->in), "cudaEventRecord");
+        CUDAIR_TRY(cudaStreamWaitEvent(s, p->block_in[i], 0), "cudaStreamWaitEvent");
+        rc = cudair_vecadd(a_dev + i0, b_dev + i0, out_dev + i0, static_cast<int32_t>(len), s);
+        if (rc != CUDAIR_OK) return rc;
+        CUDAIR_TRY(cudaEventRecord(p->block_done[i], s), "cudaEventRecord");
+        CUDAIR_TRY(cudaStreamWaitEvent(p->out, p->block_done[i], 0), "cudaStreamWaitEvent");
+        CUDAIR_TRY(cudaMemcpyAsync(out_host + i0, out_dev + i0, bytes, cudaMemcpyDeviceToHost, p->out),
+                   "D2H of out");
+        CUDAIR_TRY(cudaEventRecord(p->block_out[i], p->out), "cudaEventRecord");
+    }
+    CUDAIR_TRY(cudaStreamWaitEvent(s, p->block_out[chunks - 1], 0), "cudaStreamWaitEvent");
+#undef CUDAIR_TRY
+    return CUDAIR_OK;
+}
+
+// =============================================================================
+// MatMul16 from host buffers: advanced_test.go:466-483 (copy A, B and C in,
+// launch MatMul16, copy C back) as one call on the caller's stream.  Up to
+// n = 512 the copies and cudair_matmul16's one launch run in order (the
+// copies are a few microseconds each and there is nothing to overlap); above
+// that the pipelined cudair_gemm_f16f32_host takes over.
+// =============================================================================
+CUDAIR_API int cudair_matmul16_host(const void *a_host, const void *b_host, float *c_host, int32_t n,
+                                    void *a_dev, void *b_dev, float *c_dev, void *stream) {
+    clear_error();
+    if (n < 0 || (n & 15) != 0)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: MatMul16: n = %d, want a non-negative multiple of 16", n);
+    if (n == 0) return CUDAIR_OK;
+    if (!a_host || !b_host || !c_host || !a_dev || !b_dev || !c_dev)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: matmul16_host: nil pointer");
+    if (n > 512)
+        return cudair_gemm_f16f32_host(a_host, b_host, c_host, n, n, n, n, n, n, a_dev, b_dev, c_dev, 0, stream);
+    int rc = ensure_context();
+    if (rc != CUDAIR_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t h = static_cast<size_t>(n) * n * 2, f = static_cast<size_t>(n) * n * 4;
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(a_dev, a_host, h, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+        return cuda_error(e, "H2D of A");
+    if ((e = cudaMemcpyAsync(b_dev, b_host, h, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+        return cuda_error(e, "H2D of B");
+    if ((e = cudaMemcpyAsync(c_dev, c_host, f, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+        return cuda_error(e, "H2D of C");
+    if ((rc = cudair_matmul16(a_dev, b_dev, c_dev, n, stream)) != CUDAIR_OK) return rc;
+    if ((e = cudaMemcpyAsync(c_host, c_dev, f, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+        return cuda_error(e, "D2H of C");
     return CUDAIR_OK;
 }

@@ -40,6 +40,9 @@ SIGNATURES = {
                                            c_i64, c_vp]),
     "cudair_gemm_f16f32_host": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                         c_vp, c_vp, c_vp, c_i64, c_vp]),
+    "cudair_matmul16_host": (c_int, [c_vp, c_vp, c_vp, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp]),
+    "cudair_vecadd_host": (c_int, [c_vp, c_vp, c_vp, ctypes.c_int32, c_vp, c_vp, c_vp, ctypes.c_int32,
+                                   c_vp]),
     "cudair_gemm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                             c_u32, c_vp]),
     "cudair_set_gemm_variant": (c_int, [c_int]),

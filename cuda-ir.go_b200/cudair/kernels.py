@@ -128,6 +128,47 @@ def gemm_host(a_h, b_h, c_h, a_d, b_d, c_d, rows_per_block=0, stream=None) -> No
         _stream(stream)))
 
 
+def _host_tensor(t, dtype, name):
+    import torch
+    if not isinstance(t, torch.Tensor) or t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise CudairError(1, f"cudair: {name} must be a contiguous host {dtype} tensor")
+
+
+def vecadd_host(a_h, b_h, out_h, a_d, b_d, out_d, chunk=0, stream=None) -> None:
+    """out_h = a_h + b_h from host (CPU) fp32 vectors through the caller's
+    device buffers (cudair_vecadd_host): copies in, VecAdd and copies out
+    pipelined over chunks.  Asynchronous on `stream`; pinned host tensors let
+    the copies overlap."""
+    import torch
+    for t, nm in ((a_h, "a_h"), (b_h, "b_h"), (out_h, "out_h")):
+        _host_tensor(t, torch.float32, nm)
+    for t, nm in ((a_d, "a_d"), (b_d, "b_d"), (out_d, "out_d")):
+        _need(t, torch.float32, nm)
+    n = out_h.numel()
+    if any(t.numel() != n for t in (a_h, b_h, a_d, b_d, out_d)):
+        raise CudairError(1, "cudair: vecadd_host: length mismatch")
+    check(lib().cudair_vecadd_host(a_h.data_ptr(), b_h.data_ptr(), out_h.data_ptr(), n, a_d.data_ptr(),
+                                   b_d.data_ptr(), out_d.data_ptr(), chunk, _stream(stream)))
+
+
+def matmul16_host(a_h, b_h, c_h, a_d, b_d, c_d, stream=None) -> None:
+    """c_h += a_h @ b_h for n x n host tensors (MatMul16's operands) through
+    the caller's device buffers (cudair_matmul16_host).  Asynchronous on
+    `stream`."""
+    import torch
+    _host_tensor(a_h, torch.float16, "a_h")
+    _host_tensor(b_h, torch.float16, "b_h")
+    _host_tensor(c_h, torch.float32, "c_h")
+    _need(a_d, torch.float16, "a_d")
+    _need(b_d, torch.float16, "b_d")
+    _need(c_d, torch.float32, "c_d")
+    n = c_h.shape[0]
+    if any(tuple(t.shape) != (n, n) for t in (a_h, b_h, c_h, a_d, b_d, c_d)):
+        raise CudairError(1, "cudair: matmul16_host: every operand must be n x n")
+    check(lib().cudair_matmul16_host(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), n, a_d.data_ptr(),
+                                     b_d.data_ptr(), c_d.data_ptr(), _stream(stream)))
+
+
 def set_gemm_variant(variant: int) -> None:
     """0 = automatic, 1 = single-CTA 128x256 tiles, 2 = CTA-pair 256x256 tiles,
     3 = few-row kernel (M <= 128), 4 = CTA-pair 256x512 tiles."""

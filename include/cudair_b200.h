@@ -248,6 +248,20 @@ int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, float *c_hos
                             int64_t rows_per_block, void *stream);
 
 /*
+ * MatMul16 from host buffers: the whole flow of the reference's MatMul16
+ * test (advanced_test.go:466-483: CopyFrom of A, B and C, the launch, CopyTo
+ * of C) as one call.  a_host, b_host (n x n fp16) and c_host (n x n fp32)
+ * are host memory (page-locked for asynchronous copies); a_dev, b_dev and
+ * c_dev are the caller's device buffers of the same sizes.  Up to n = 512
+ * the three copies in, cudair_matmul16 and the copy out run in order on
+ * `stream`; above that the call is cudair_gemm_f16f32_host.  Asynchronous:
+ * once `stream` is synchronised, c_host holds C = A.B + C.  Allocates
+ * nothing.
+ */
+int cudair_matmul16_host(const void *a_host, const void *b_host, float *c_host, int32_t n,
+                         void *a_dev, void *b_dev, float *c_dev, void *stream);
+
+/*
  * The few-row GEMM (1 <= M <= 64, N <= 524288) without any device
  * allocation.  No counterpart in the reference: it serves hosts that must not
  * allocate device memory themselves, because another allocator owns all of
@@ -273,6 +287,20 @@ int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c,
  * as they finish.  Any alignment is accepted.  Asynchronous.
  */
 int cudair_vecadd(const float *a, const float *b, float *out, int32_t n, void *stream);
+
+/*
+ * VecAdd from host buffers: the flow of the reference's TestVecAdd
+ * (main_test.go:31-48: upload a and b, launch VecAdd, copy out back) as one
+ * call.  a_host, b_host, out_host are host memory (page-locked for the copies
+ * to overlap); a_dev, b_dev, out_dev are the caller's device buffers of n
+ * floats.  The vectors travel in chunks of `chunk` elements (0: about
+ * sixteen chunks of at least 2^20 elements; at most 64 chunks): chunk i+1 is
+ * copied in on a library-owned stream while chunk i is added on `stream` and
+ * chunk i-1 is copied out on another.  Asynchronous: once `stream` is
+ * synchronised, out_host holds a + b, bit-exact.  Allocates nothing.
+ */
+int cudair_vecadd_host(const float *a_host, const float *b_host, float *out_host, int32_t n,
+                       float *a_dev, float *b_dev, float *out_dev, int32_t chunk, void *stream);
 
 /*
  * The rest of the vecadd package (vecadd.go:13-28), streamed like VecAdd in

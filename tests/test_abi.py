@@ -216,6 +216,20 @@ def test_saxpy_and_square_validation(cudair):
     assert "Square: nil pointer" in cudair.last_error()
 
 
+def test_host_entries_validation(cudair):
+    L = cudair.lib()
+    assert L.cudair_vecadd_host(None, None, None, -1, None, None, None, 0, None) == 1
+    assert L.cudair_vecadd_host(None, None, None, 16, None, None, None, -1, None) == 1
+    assert L.cudair_vecadd_host(None, None, None, 0, None, None, None, 0, None) == 0
+    assert L.cudair_vecadd_host(None, None, None, 16, None, None, None, 0, None) == 1
+    assert "vecadd_host: nil pointer" in cudair.last_error()
+    assert L.cudair_matmul16_host(None, None, None, 24, None, None, None, None) == 1
+    assert "multiple of 16" in cudair.last_error()
+    assert L.cudair_matmul16_host(None, None, None, 0, None, None, None, None) == 0
+    assert L.cudair_matmul16_host(None, None, None, 32, None, None, None, None) == 1
+    assert "matmul16_host: nil pointer" in cudair.last_error()
+
+
 def test_fill_validation(cudair):
     # Checked before the device is touched.
     L = cudair.lib()
