@@ -34,6 +34,7 @@ struct Driver {
     CUresult (*cuCtxGetCurrent)(CUcontext *);
     CUresult (*cuCtxSetCurrent)(CUcontext);
     CUresult (*cuCtxSynchronize)(void);
+    CUresult (*cuDevicePrimaryCtxRetain)(CUcontext *, CUdevice);
     CUresult (*cuModuleLoadData)(CUmodule *, const void *);
     CUresult (*cuModuleUnload)(CUmodule);
     CUresult (*cuModuleGetFunction)(CUfunction *, CUmodule, const char *);
@@ -63,6 +64,9 @@ int encode_tiled_internal(CUtensorMap *out, uint32_t data_type, uint32_t rank,
                           const uint32_t *element_strides, uint32_t interleave, uint32_t swizzle,
                           uint32_t l2_promotion, uint32_t oob_fill);
 
+// Both also check the device (compute capability 10.0) and that the current
+// context is the device's primary context, where the library's per-device
+// state (symbol addresses, workspaces, streams, events) lives.
 int sm_count_current_device(int *count);
 // Device address of the bounded-wait status word on the current device.
 int wait_status_current_device(unsigned int **status);

@@ -83,6 +83,7 @@ void open_driver() {
         bind(h, g_drv.cuCtxGetCurrent, "cuCtxGetCurrent") &&
         bind(h, g_drv.cuCtxSetCurrent, "cuCtxSetCurrent") &&
         bind(h, g_drv.cuCtxSynchronize, "cuCtxSynchronize") &&
+        bind(h, g_drv.cuDevicePrimaryCtxRetain, "cuDevicePrimaryCtxRetain") &&
         bind(h, g_drv.cuModuleLoadData, "cuModuleLoadData") &&
         bind(h, g_drv.cuModuleUnload, "cuModuleUnload") &&
         bind(h, g_drv.cuModuleGetFunction, "cuModuleGetFunction") &&

@@ -536,8 +536,16 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
 // serving, because cudaMalloc may synchronise the device and stall every
 // other stream.  cudair_gemm_f16f32 allocates the few-row kernel's 21 MB
 // workspace on its first call on a device; this entry point instead keeps
-// that scratch space in a fixed array in the library's own device memory,
-// reserved when the library is loaded, so no call ever allocates.
+// that scratch space in a fixed array that is part of the library's device
+// image.  The CUDA runtime reserves the array in a device's memory when it
+// loads that image into the device's context.  Under lazy module loading
+// (the runtime's default since CUDA 12.2) that happens on first use, which
+// for this array is this entry's first call on the device (it looks up the
+// array's address), unless another call of the library on that device loaded
+// the image before.  So a caller that must not allocate after start-up makes
+// one call per device at start-up (or runs with CUDA_MODULE_LOADING=EAGER,
+// which loads the image when the context is created); later calls reserve
+// nothing.
 // =============================================================================
 
 namespace cudair {
@@ -561,7 +569,9 @@ namespace {
 
 // Host code cannot use g_noalloc_scratch as a pointer: on the host the name
 // only stands in for the device variable.  The device address is looked up
-// once per device, with that device current, and cached.
+// once per device, with that device current, and cached.  It is the address
+// in the device's primary context; the entry point runs only there
+// (sm_count_current_device refuses any other context first).
 std::mutex g_noalloc_mu;
 unsigned char *g_noalloc_ptr[64];
 bool g_noalloc_attr[64];
@@ -595,8 +605,10 @@ int noalloc_scratch(unsigned char **out) {
 // C (M x N) += A (M x K) . B (K x N) for 1 <= M <= 64 and N <= 524288, with
 // the same operands, layout rules and results as cudair_gemm_f16f32 (up to
 // fp32 rounding order), without allocating.  The first call on a device looks
-// up the scratch array's address and sets the kernel's shared-memory limit;
-// make that first call before any stream capture.  Each call clears the tile
+// up the scratch array's address (under lazy module loading, this is when the
+// runtime loads the image and reserves the array) and sets the kernel's
+// shared-memory limit; make that first call at start-up, before any stream
+// capture.  Each call clears the tile
 // counters it uses (cudaMemsetAsync on `stream`) and then launches; all calls
 // share the one array, so calls that overlap on the GPU (e.g. on different
 // streams at once) race and must be avoided.  With M > 16 the kernel runs on

@@ -746,6 +746,7 @@ struct DeviceInfo {
     int major = 0, minor = 0;
     int max_pairs = 0;  // CTA pairs resident at once
     unsigned int *status = nullptr;  // device address of g_wait_status
+    CUcontext primary = nullptr;     // the device's primary context (retained)
     bool attr_set = false;
 };
 
@@ -773,6 +774,27 @@ int device_info(DeviceInfo **out) {
         return set_error(CUDAIR_ERR_UNSUPPORTED,
                          "cudair: device %d has compute capability %d.%d; this build targets sm_100a (10.0)",
                          dev, d.major, d.minor);
+    // The library's per-device state (the addresses of its __device__
+    // variables, workspaces, streams, events) belongs to one context per
+    // device: the primary context, which the runtime and gocudrv use.  A call
+    // made with another context current is refused instead of handing its
+    // kernels addresses from the primary context.
+    const Driver *drv = nullptr;
+    int rc = load_driver(&drv);
+    if (rc != CUDAIR_OK) return rc;
+    if ((rc = ensure_context()) != CUDAIR_OK) return rc;
+    if (!d.primary) {
+        CUresult r = drv->cuDevicePrimaryCtxRetain(&d.primary, static_cast<CUdevice>(dev));
+        if (r != CUDA_SUCCESS) return cu_error(r, "cuDevicePrimaryCtxRetain");
+    }
+    CUcontext cur = nullptr;
+    CUresult r = drv->cuCtxGetCurrent(&cur);
+    if (r != CUDA_SUCCESS) return cu_error(r, "cuCtxGetCurrent");
+    if (cur != d.primary)
+        return set_error(CUDAIR_ERR_UNSUPPORTED,
+                         "cudair: the current context is not device %d's primary context; the library "
+                         "runs in the primary context only (the one the CUDA runtime and gocudrv use)",
+                         dev);
     if (!d.attr_set) {
         const struct {
             const void *fn;
@@ -1073,6 +1095,9 @@ CUDAIR_API int cudair_matmul16(const void *a, const void *b, float *c, int32_t n
         if (!a || !b || !c) return set_error(CUDAIR_ERR_INVALID, "cudair: MatMul16: nil pointer");
         if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u)
             return set_error(CUDAIR_ERR_INVALID, "cudair: MatMul16: A and B must be 16-byte aligned");
+        int sms = 0;
+        int rc = sm_count_current_device(&sms);  // the device and context checks
+        if (rc != CUDAIR_OK) return rc;
         return matmul16_warp_launch(a, b, c, n, static_cast<cudaStream_t>(stream));
     }
     return gemm_f16f32_launch(a, b, c, n, n, n, n, n, n, static_cast<cudaStream_t>(stream));

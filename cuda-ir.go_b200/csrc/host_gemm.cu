@@ -132,7 +132,8 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
         rb = ((M + kMaxBlocks / col_blocks - 1) / (kMaxBlocks / col_blocks) + 255) / 256 * 256;
     const int row_blocks = static_cast<int>((M + rb - 1) / rb);
 
-    int rc = ensure_context();
+    int sms = 0;
+    int rc = sm_count_current_device(&sms);  // device and primary-context checks
     if (rc != CUDAIR_OK) return rc;
     std::lock_guard<std::mutex> lk(g_pipe_mu);  // the events are shared per device
     HostPipe *p = nullptr;
@@ -221,7 +222,8 @@ CUDAIR_API int cudair_vecadd_host(const float *a_host, const float *b_host, floa
     if ((n + ch - 1) / ch > kMaxBlocks) ch = ((n + kMaxBlocks - 1) / kMaxBlocks + 3) / 4 * 4;
     const int chunks = static_cast<int>((n + ch - 1) / ch);
 
-    int rc = ensure_context();
+    int sms = 0;
+    int rc = sm_count_current_device(&sms);  // device and primary-context checks
     if (rc != CUDAIR_OK) return rc;
     std::lock_guard<std::mutex> lk(g_pipe_mu);
     HostPipe *p = nullptr;
@@ -272,7 +274,8 @@ CUDAIR_API int cudair_matmul16_host(const void *a_host, const void *b_host, floa
         return set_error(CUDAIR_ERR_INVALID, "cudair: matmul16_host: nil pointer");
     if (n > 512)
         return cudair_gemm_f16f32_host(a_host, b_host, c_host, n, n, n, n, n, n, a_dev, b_dev, c_dev, 0, stream);
-    int rc = ensure_context();
+    int sms = 0;
+    int rc = sm_count_current_device(&sms);  // device and primary-context checks
     if (rc != CUDAIR_OK) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t h = static_cast<size_t>(n) * n * 2, f = static_cast<size_t>(n) * n * 4;

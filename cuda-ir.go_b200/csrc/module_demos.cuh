@@ -130,9 +130,10 @@ extern "C" __global__ void TmaDouble(const int *in, int *out, int n) {
     using namespace cudair_demo;
     __shared__ __align__(128) int tile[kBlock];
     __shared__ uint64_t bar;
+    __shared__ int landed;
     const int tid = threadIdx.x;
     const int base = blockIdx.x * kBlock;
-    if (base >= n) return;
+    if (base >= n) return;  // the whole block, before any barrier
     if (tid == 0) {
         mbar_init(&bar, 1);
         fence_mbar_init();
@@ -147,9 +148,16 @@ extern "C" __global__ void TmaDouble(const int *in, int *out, int n) {
                 s_addr(tile)),
             "l"(in + base), "r"(static_cast<uint32_t>(kBlock * sizeof(int))), "r"(s_addr(&bar))
             : "memory");
+        landed = mbar_wait_parity(&bar, 0) ? 1 : 0;
+        // A wait that gave up leaves the copy in flight, writing this block's
+        // shared memory: wait for it once more (bounded) before the block
+        // leaves.
+        if (!landed) mbar_wait_parity(&bar, 0);
     }
-    const bool landed = mbar_wait_parity(&bar, 0);
-    if (!landed) return;  // the copy's bytes are counted on `bar`; nothing else reads the tile
+    // One thread decides for the block, so the barrier below is reached by
+    // every thread and the early return is the whole block's.
+    __syncthreads();
+    if (!landed) return;
     if (tid < kBlock) tile[tid] *= 2;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async proxy
     __syncthreads();
@@ -212,9 +220,12 @@ extern "C" __global__ void TensorTileDouble(const CUtensorMap *src, const CUtens
             "l"(reinterpret_cast<uint64_t>(src)), "r"(x0), "r"(y0), "r"(s_addr(&bar))
             : "memory");
         landed = mbar_wait_parity(&bar, 0) ? 1 : 0;
+        // As in TmaDouble: a load still in flight is waited for (bounded)
+        // before the block leaves.
+        if (!landed) mbar_wait_parity(&bar, 0);
     }
     __syncthreads();
-    if (!landed) return;
+    if (!landed) return;  // the whole block: every thread read the flag after the barrier
     for (int i = tid; i < kTile * kTile; i += blockDim.x) t[i] *= 2.0f;
     __syncthreads();
     if (tid == 0) {

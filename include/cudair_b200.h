@@ -25,10 +25,12 @@
  * Conventions: every function returns CUDAIR_OK (0) or an error code; the
  * message of the calling thread's last error is cudair_last_error().  Device
  * pointers are passed as plain pointers / uint64_t.  A NULL stream is the
- * legacy default stream.  Calls use the CUDA context current on the calling
- * thread, making the device's primary context current when there is none
- * (the context gocudrv itself uses).  No function allocates device memory
- * unless its comment says so; the caller owns every buffer.
+ * legacy default stream.  Calls run in the current device's primary context
+ * (the context gocudrv and the CUDA runtime use), making it current when no
+ * context is; a call made while another context is current returns
+ * CUDAIR_ERR_UNSUPPORTED, since the library's per-device state lives in the
+ * primary context.  No function allocates device memory unless its comment
+ * says so; the caller owns every buffer.
  */
 #ifndef CUDAIR_B200_H
 #define CUDAIR_B200_H
@@ -271,10 +273,15 @@ int cudair_matmul16_host(const void *a_host, const void *b_host, float *c_host, 
  * are those of cudair_gemm_f16f32 (up to fp32 rounding order).  Its scratch
  * space is a fixed 4 MiB + 16 KiB array in the library's device image, held
  * on every GPU that loads the library until exit; sizes beyond the maximum
- * return CUDAIR_ERR_INVALID.  The first call on a device looks up the array's
- * address and sets the kernel's shared-memory limit (make it before any stream
- * capture); every call clears the tile counters it uses and then launches.
- * All calls share the array: calls that overlap on the GPU race.
+ * return CUDAIR_ERR_INVALID.  The runtime reserves the array when it loads
+ * the image on a device; under lazy module loading (the default since CUDA
+ * 12.2) that is the first use, normally this entry's first call on the
+ * device.  So make one call per device at start-up, before any stream
+ * capture (or set CUDA_MODULE_LOADING=EAGER): that first call looks up the
+ * array's address and sets the kernel's shared-memory limit, and no later
+ * call reserves anything.  Every call clears the tile counters it uses and
+ * then launches.  All calls share the array: calls that overlap on the GPU
+ * race.
  */
 int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c,
                                int64_t M, int64_t N, int64_t K,
