@@ -951,12 +951,12 @@ def run_ours(args, world, rank, local):
     if only == "gemm":
         return
 
+    # The strong-scaling GEMMs run at the power limit; the host-link-bound
+    # e2e leg after them lets the clocks recover before the HBM-bound legs.
+    strong = run_strong(world, rank, dev, kernels, b if data is SHARDED else None)
     e2e = run_e2e(args, world, rank, dev, a, b, c, flops, kernels)
     gather = run_gather(world, dev, c) if world > 1 else None
-    del a, c
-    torch.cuda.empty_cache()
-    strong = run_strong(world, rank, dev, kernels, b if data is SHARDED else None)
-    del b
+    del a, b, c
     torch.cuda.empty_cache()
     vecadd = run_vecadd(args, world, rank, dev, kernels, peaks, traffic)
     streams = run_saxpy_square(args, world, rank, dev, kernels, peaks)
