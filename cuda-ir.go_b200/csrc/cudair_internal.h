@@ -82,6 +82,14 @@ int gemm_pdl_mode();
 // The one-warp-per-tile MatMul16 (square n, a multiple of 16; row-major, ld = n).
 int matmul16_warp_launch(const void *a, const void *b, float *c, int n, cudaStream_t stream);
 
+// The small-problem kernel (gemm_small_sm100.cu): one 128 x 64 tile of C per
+// CTA, the whole K panel (K <= 64 * kSmallMaxKBlocks) loaded at once.  Takes
+// the tensor maps the square-tile kernels use (A: box 64 k x 128 rows, B:
+// box 64 n x 64 k, 128-byte swizzle) and the plain form only.
+constexpr int kSmallMaxKBlocks = 8;
+int gemm_small_launch(const CUtensorMap &tmA, const CUtensorMap &tmB, float *c, int64_t M, int64_t N,
+                      int64_t K, int64_t ldc, unsigned int *status, cudaStream_t stream);
+
 int gemm_f16f32_launch(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K,
                        int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t stream);
 

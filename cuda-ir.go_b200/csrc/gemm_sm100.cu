@@ -1009,6 +1009,11 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
     if (variant == 3 && flags != 0)
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm: the few-row kernel (variant 3) takes only the plain form (flags 0)");
+    if (variant == 5 && (flags != 0 || K > 64 * kSmallMaxKBlocks))
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm: the small-problem kernel (variant 5) takes the plain form (flags 0) "
+                         "and K <= %d",
+                         64 * kSmallMaxKBlocks);
     // It also needs at least one (128-column x 64-k) unit of work per SM: on
     // fewer it leaves SMs idle and pays its fix-up anyway (128^3: 14.1 us
     // against 5.3 us for the single-CTA kernel).
@@ -1062,6 +1067,7 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
         if (rc != CUDAIR_OK) return rc;
     }
     float *cf = static_cast<float *>(c);
+    if (variant == 5) return gemm_small_launch(tmA, tmB, cf, M, N, K, ldc, dev->status, stream);
     const bool pdl = g_pdl.load() > 0;
     e = bt ? launch_square<true>(nb, *dev, tmA, tmB, tmC, cf, M, N, K, static_cast<long long>(ldc), bf16, epi,
                                  pdl, stream)
@@ -1135,10 +1141,10 @@ CUDAIR_API int cudair_gemm(const void *a, const void *b, void *c, const float *b
 
 CUDAIR_API int cudair_set_gemm_variant(int variant) {
     clear_error();
-    if (variant < 0 || variant > 4)
+    if (variant < 0 || variant > 5)
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm variant %d, want 0 (auto), 1 (single CTA), 2 (CTA pair), "
-                         "3 (few rows) or 4 (CTA pair, 256 x 512 tiles)",
+                         "3 (few rows), 4 (CTA pair, 256 x 512 tiles) or 5 (small problems, K <= 512)",
                          variant);
     g_variant.store(variant);
     return CUDAIR_OK;

@@ -33,20 +33,23 @@ def no_wait_timeouts(dev, cudair):
     assert kernels.wait_status(clear=True) == 0
 
 
-@pytest.fixture(params=[1, 2, 3, 4], ids=["single", "pair", "fewrows", "pairwide"])
+@pytest.fixture(params=[1, 2, 3, 4, 5], ids=["single", "pair", "fewrows", "pairwide", "small"])
 def variant(request, dev, cudair):
     """Runs a test on each GEMM kernel in turn: single CTA (128x256 tiles),
-    CTA pair (256x256), the few-row kernel (M <= 128) and the wide CTA pair
-    (256x512), then restores the automatic choice."""
+    CTA pair (256x256), the few-row kernel (M <= 128), the wide CTA pair
+    (256x512) and the small-problem kernel (K <= 512, one 128x64 tile per
+    CTA), then restores the automatic choice."""
     from cudair import kernels
     kernels.set_gemm_variant(request.param)
     yield request.param
     kernels.set_gemm_variant(0)
 
 
-def _applies(variant, M):
+def _applies(variant, M, K=0):
     if variant == 3 and M > 128:
         pytest.skip("the few-row kernel takes M <= 128")
+    if variant == 5 and K > 512:
+        pytest.skip("the small-problem kernel takes K <= 512")
 
 
 def kat(M, N, K):
@@ -117,7 +120,7 @@ def test_matmul16_reference_launch_seeded_n256(dev, module, oracle, golden_dir):
 def test_matmul16_tcgen05_kat_exact(dev, cudair, variant, n):
     import torch
     from cudair import kernels
-    _applies(variant, n)
+    _applies(variant, n, n)
     af, bf, c, want = kat(n, n, n)
     da, db, dc = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16), _dev(c, dev, torch.float32)
     kernels.matmul16(da, db, dc)
@@ -156,7 +159,7 @@ def test_matmul16_tcgen05_seeded_n256(dev, cudair, oracle, golden_dir):
 def test_gemm_tcgen05_ragged_kat_exact(dev, cudair, variant, M, N, K):
     import torch
     from cudair import kernels
-    _applies(variant, M)
+    _applies(variant, M, K)
     af, bf, c, want = kat(M, N, K)
     da, db, dc = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16), _dev(c, dev, torch.float32)
     kernels.gemm(da, db, dc)
@@ -195,7 +198,7 @@ def test_gemm_8192_cube_seeded(dev, cudair, oracle, variant):
     import torch
     from cudair import kernels
     n = 8192
-    _applies(variant, n)
+    _applies(variant, n, n)
     a16, af = _seeded_normal_f16(oracle, n * n, 6, 1.0 / np.sqrt(n))
     b16, bf = _seeded_normal_f16(oracle, n * n, 7, 1.0 / np.sqrt(n))
     c = oracle.normal(n * n, 8).reshape(n, n)
