@@ -1020,6 +1020,13 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
     const int64_t units = ((N + 127) / 128) * ((K + 63) / 64);
     const bool fewrows_auto = variant == 0 && flags == 0 && (M <= 64 || (M <= 128 && N <= 8192)) &&
                               units >= dev->sm_count;
+    // A problem of one wave of the small-problem kernel's 128 x 64 tiles
+    // with K <= 512 takes that kernel: the whole K panel is loaded at once,
+    // and the pipelined kernels' set-up would not be amortised.
+    const int64_t small_tiles = ((M + 127) / 128) * ((N + 63) / 64);
+    const bool small_auto = variant == 0 && flags == 0 && !fewrows_auto && K <= 64 * kSmallMaxKBlocks &&
+                            small_tiles <= dev->sm_count;
+    const int use_variant = small_auto ? 5 : variant;
     if (variant == 3 || fewrows_auto)
         return gemm_skinny_launch(a, b, static_cast<float *>(c), static_cast<int>(M), static_cast<int>(N),
                                   static_cast<int>(K), lda, ldb, ldc, dev->sm_count, dev->status,
@@ -1067,7 +1074,7 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
         if (rc != CUDAIR_OK) return rc;
     }
     float *cf = static_cast<float *>(c);
-    if (variant == 5) return gemm_small_launch(tmA, tmB, cf, M, N, K, ldc, dev->status, stream);
+    if (use_variant == 5) return gemm_small_launch(tmA, tmB, cf, M, N, K, ldc, dev->status, stream);
     const bool pdl = g_pdl.load() > 0;
     e = bt ? launch_square<true>(nb, *dev, tmA, tmB, tmC, cf, M, N, K, static_cast<long long>(ldc), bf16, epi,
                                  pdl, stream)
@@ -1093,11 +1100,12 @@ CUDAIR_API int cudair_matmul16(const void *a, const void *b, float *c, int32_t n
     if (n == 0) return CUDAIR_OK;
     if ((reinterpret_cast<uintptr_t>(c) & 15u) != 0)
         return set_error(CUDAIR_ERR_INVALID, "cudair: MatMul16: C must be 16-byte aligned");
-    // Up to n = 512 the one-warp-per-tile kernel has the lower latency (a
-    // few pair tiles cannot amortise the pipelined kernels' set-up: n = 256
-    // 3.6 against 7.8 us, n = 512 8.9 against 9.4 us, n = 768 25.5 against
-    // 10.6 us).
-    if (n <= 512 && g_variant.load() == 0) {
+    // Up to n = 384 the one-warp-per-tile kernel has the lowest latency
+    // (n = 256: 3.5 us, against 4.9 us for the small-problem tcgen05 kernel
+    // and 7.7 us for the pipelined ones); from there to n = 512 the
+    // small-problem kernel (n = 512: 5.7 against 9.0 us), which the GEMM's
+    // automatic choice takes for K <= 512.
+    if (n <= 384 && g_variant.load() == 0) {
         if (!a || !b || !c) return set_error(CUDAIR_ERR_INVALID, "cudair: MatMul16: nil pointer");
         if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u)
             return set_error(CUDAIR_ERR_INVALID, "cudair: MatMul16: A and B must be 16-byte aligned");

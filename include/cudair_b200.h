@@ -140,10 +140,12 @@ int cudair_ctx_synchronize(void);
  * C = A.B + C for n x n row-major matrices: fp16 A and B, fp32 C updated in
  * place, fp32 accumulation.  Same operands as MatMul16 (hopper.go:201); this
  * launcher runs the sm_100a tcgen05/TMA kernel on a persistent grid instead
- * of the reference's one-warp-per-16x16-tile launch when n > 512; for
- * n <= 512 it launches that warp-per-tile kernel itself, whose latency is the
- * lower one there (n = 256: 3.6 against 7.8 us).  n must be a multiple of
- * 16 (the reference's own requirement) and the pointers 16-byte aligned.
+ * of the reference's one-warp-per-16x16-tile launch when n > 384: the
+ * small-problem kernel (whole K panel by TMA, one 128 x 64 tile per CTA) up
+ * to n = 512, the persistent CTA-pair kernels above; for n <= 384 it
+ * launches the warp-per-tile kernel itself, whose latency is the lowest
+ * there (n = 256: 3.5 us).  n must be a multiple of 16 (the reference's own
+ * requirement) and the pointers 16-byte aligned.
  * Asynchronous on stream.
  */
 int cudair_matmul16(const void *a, const void *b, float *c, int32_t n, void *stream);
@@ -191,12 +193,15 @@ int cudair_gemm(const void *a, const void *b, void *c, const float *bias,
 /*
  * Selects the GEMM kernel variant for subsequent calls in this process:
  * 0 = automatic (few-row kernel when M <= 64, and when M <= 128 with
- * N <= 8192; single CTAs with 128 x 256 tiles for the rest of M <= 128;
- * else CTA pairs with 256 x 256 or 256 x 512 tiles, whichever a makespan
- * estimate for the shape favours), 1 = single CTA, 2 = CTA pair
- * with 256 x 256 tiles, 3 = few-row kernel (M <= 128 only), 4 = CTA pair
- * with 256 x 512 tiles.  All variants compute the same result within fp32
- * rounding; the choice only affects speed.
+ * N <= 8192, given one 128-column x 64-k unit of work per SM; the
+ * small-problem kernel when K <= 512 and its 128 x 64 tiles fit one wave;
+ * single CTAs with 128 x 256 tiles for the rest of M <= 128; else CTA pairs
+ * with 256 x 256 or 256 x 512 tiles, whichever a makespan estimate for the
+ * shape favours), 1 = single CTA, 2 = CTA pair with 256 x 256 tiles,
+ * 3 = few-row kernel (M <= 128 only), 4 = CTA pair with 256 x 512 tiles,
+ * 5 = small-problem kernel (K <= 512; one 128 x 64 tile of C per CTA, the
+ * whole K panel loaded at once).  All variants compute the same result
+ * within fp32 rounding; the choice only affects speed.
  *
  * The few-row kernel (B as the MMA's 128-row side, K split evenly over all
  * SMs) keeps its partial sums and tile counters in a 21.25 MB per-device

@@ -373,3 +373,32 @@ def test_fewrows_contributors_per_tile(dev, cudair, M, kb):
                 assert np.all(got[:, N:] == -9.0)
     finally:
         kernels.set_gemm_variant(0)
+
+
+@pytest.mark.parametrize("M", [1, 5, 16, 40, 64])
+@pytest.mark.parametrize("N,K", [(14336, 4096), (9416, 1000), (18816, 136), (12000, 64), (10000, 4104)])
+def test_fewrows_64_column_tiles(dev, cudair, M, N, K):
+    # Shapes with fewer 128-column tiles than SMs but at least as many
+    # 64-column ones take the few-row kernel's 64-column tiles (MMA M = 64,
+    # 128-wide k units): the decode shape, exactly one tile per CTA
+    # (N = 9416), ragged N and K (a k unit half or wholly beyond K), K under
+    # one unit.  Exact (integer data), twice in a row from the same C
+    # (bit-identical), and C's padding columns untouched.
+    import torch
+    from cudair import kernels
+    kernels.set_gemm_variant(3)
+    try:
+        af, bf, c, want = kat(M, N, K)
+        da = _dev(af, dev, torch.float16)
+        db = _dev(bf, dev, torch.float16)
+        ldc = N + 4
+        for _ in range(2):
+            C = torch.full((M, ldc), -9.0, dtype=torch.float32, device=dev)
+            C[:, :N] = _dev(c, dev, torch.float32)
+            kernels.gemm(da, db, C[:, :N])
+            got = C.cpu().numpy()
+            bad = np.argwhere(got[:, :N] != want)
+            assert bad.size == 0, (N, K, len(bad), tuple(bad[0]))
+            assert np.all(got[:, N:] == -9.0)
+    finally:
+        kernels.set_gemm_variant(0)
