@@ -4,26 +4,14 @@
 // B (K x N fp16) through HBM.
 //
 // Design:
-//   * swap of operands: D^T (N x M) = B^T . A^T, so the row side of
-//     tcgen05.mma runs over N and the small M becomes the MMA's N (mpad = M
-//     rounded up to 16).  B is read MN-major exactly as stored, A K-major.
-//   * stream-K: the (n-tile x k-unit) space is cut into one contiguous range
-//     per CTA, one CTA per SM, so every SM streams the same share of B however
-//     N and K divide.  A range covers whole n-tiles (written straight into C)
-//     and at most two partial ones.
-//   * two tile widths, chosen per call:
-//       TN = 128: 128-column tiles (MMA M = 128), 64-wide k units;
-//       TN =  64: 64-column tiles (MMA M = 64), 128-wide k units, for shapes
-//         with fewer 128-column tiles than SMs (the decode shape: 112 tiles on
-//         148 SMs).  There, each CTA's range is longer than a tile, so every
-//         range crosses a tile boundary and every partial tile has exactly
-//         two contributors: the CTA that starts its range with the tile's
-//         tail (and publishes it early) and the CTA that ends its range with
-//         the tile's head (and finishes it).  With 128-column tiles some
-//         ranges lie inside one tile, and such a tile has two contributors
-//         that both finish at the end of the launch, which chains their
-//         hand-over (publish, count, read) onto the launch's tail.
-//     Both move 16 KB of B per stage.
+//   * swap of operands: D^T (N x M) = B^T . A^T, so the 128-row side of
+//     tcgen05.mma (M = 128) runs over N and the small M becomes the MMA's N
+//     (mpad = M rounded up to 16).  B is read MN-major exactly as stored, A
+//     K-major; the accumulator is 128 TMEM lanes (n) x mpad columns (m).
+//   * stream-K: the (n-tile x 64-wide k-block) space is cut into one
+//     contiguous range per CTA, one CTA per SM, so every SM streams the same
+//     share of B however N and K divide.  A range covers whole n-tiles
+//     (written straight into C) and at most two partial ones.
 //   * deterministic fix-up: a partial n-tile's contributors store their
 //     fp32 partials in a workspace, count themselves on the tile's counter,
 //     and the last to arrive adds C and the partials in CTA order (so the sum
@@ -31,9 +19,9 @@
 //     the counter to zero for the next launch.  The last contributor checks
 //     the counter first and, when it is last, adds its own part straight from
 //     TMEM without storing it.
-//   * a TMA ring of 16 KB B stages plus this M's A boxes, as many stages as
-//     fit (11 or 12 at M <= 16, 7 at M = 128), keeps up to 192 KB of B in
-//     flight per SM.
+//   * a TMA ring of 16 KB B tiles (two 64 x 64 boxes) plus mpad x 64 A tiles,
+//     as many stages as fit (12 at M <= 16, 7 at M = 128), keeps up to
+//     192 KB of B in flight per SM.
 //
 // Roles as in gemm_sm100.cu (192 threads): warp 0 TMA producer, warp 1 TMEM
 // owner and MMA issuer, warps 2-5 epilogue and fix-up.  All waits are
@@ -50,39 +38,28 @@ namespace cudair {
 
 namespace skinny {
 
+constexpr int BN_T = 128;  // n per tile (the MMA's M)
+constexpr int BK = 64;
 constexpr int MAX_STAGES = 12;
 constexpr int THREADS = 192;
 constexpr int MAX_M = 128;
-constexpr uint32_t B_STAGE_BYTES = 16 * 1024;  // 64 x 128 or 128 x 64 fp16
-constexpr uint32_t B_BOX_BYTES = 64 * 64 * 2;  // one 64 n x 64 k box
+constexpr uint32_t B_BOX_BYTES = 64 * BK * 2;        // 64 n x 64 k
+constexpr uint32_t B_STAGE_BYTES = 2 * B_BOX_BYTES;  // 16 KB
 constexpr uint32_t BAR_BYTES = 256;
 constexpr size_t SMEM_BYTES = 227 * 1024;  // the launch's dynamic shared memory limit
 
-// Per tile width: k per unit (one ring stage) and A bytes per stage.
-template <int TN>
-struct Tile {
-    static_assert(TN == 64 || TN == 128, "tile width");
-    static constexpr int KU = TN == 128 ? 64 : 128;  // k per unit
-    static constexpr int A_BOXES = KU / 64;          // 64-wide A boxes per stage
-    __host__ __device__ static constexpr uint32_t a_stage_bytes(int mpad) {
-        return static_cast<uint32_t>(mpad) * KU * 2;
-    }
-    // The ring holds as many stages as fit beside the barriers.
-    __host__ __device__ static constexpr int stages(int mpad) {
-        return static_cast<int>((SMEM_BYTES - 1024 - BAR_BYTES) / (B_STAGE_BYTES + a_stage_bytes(mpad))) < MAX_STAGES
-                   ? static_cast<int>((SMEM_BYTES - 1024 - BAR_BYTES) / (B_STAGE_BYTES + a_stage_bytes(mpad)))
-                   : MAX_STAGES;
-    }
-    __host__ __device__ static constexpr size_t smem(int mpad) {
-        return 1024 + static_cast<size_t>(stages(mpad)) * (B_STAGE_BYTES + a_stage_bytes(mpad)) + BAR_BYTES;
-    }
-    // fp32 partial sums of one contributor: TN x mpad.
-    __host__ __device__ static constexpr size_t slot_bytes(int mpad) {
-        return static_cast<size_t>(TN) * mpad * sizeof(float);
-    }
-};
-static_assert(Tile<128>::smem(16) <= SMEM_BYTES && Tile<128>::smem(MAX_M) <= SMEM_BYTES, "smem budget");
-static_assert(Tile<64>::smem(16) <= SMEM_BYTES && Tile<64>::smem(MAX_M) <= SMEM_BYTES, "smem budget");
+// The ring holds as many stages of (B tile + this M's A tile) as fit: with
+// M <= 16 that is 12 stages (192 KB of B in flight per SM), with M = 64 nine,
+// with M = 128 seven.
+__host__ __device__ constexpr int stages_for(int mpad) {
+    return static_cast<int>((SMEM_BYTES - 1024 - BAR_BYTES) / (B_STAGE_BYTES + mpad * BK * 2)) < MAX_STAGES
+               ? static_cast<int>((SMEM_BYTES - 1024 - BAR_BYTES) / (B_STAGE_BYTES + mpad * BK * 2))
+               : MAX_STAGES;
+}
+__host__ __device__ constexpr size_t smem_for(int mpad) {
+    return 1024 + static_cast<size_t>(stages_for(mpad)) * (B_STAGE_BYTES + mpad * BK * 2) + BAR_BYTES;
+}
+static_assert(smem_for(16) <= SMEM_BYTES && smem_for(MAX_M) <= SMEM_BYTES, "shared memory budget");
 static_assert(2 * MAX_STAGES * 8 + 5 * 8 + 12 <= BAR_BYTES, "barrier area");
 
 // Workspace layout: tile counters first, then two partial slots per CTA.
@@ -91,26 +68,22 @@ constexpr int MAX_TILES = COUNTER_BYTES / 4;
 __device__ __forceinline__ long long range_start(int c, long long T, int G) {
     return (static_cast<long long>(c) * T) / G;
 }
-// The CTA whose range contains unit x.
+// The CTA whose range contains k-block unit x.
 __device__ __forceinline__ int cta_of(long long x, long long T, int G) {
     return static_cast<int>(((x + 1) * G - 1) / T);
 }
 
-template <int TN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA,
                        float *__restrict__ C, int M, int N, int K, long long ldc, int mpad,
                        unsigned int *__restrict__ counters, float *__restrict__ partials,
                        unsigned int *status, int b_early) {
-    using T_ = Tile<TN>;
-    constexpr int KU = T_::KU;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
 
-    const uint32_t a_stage_bytes = T_::a_stage_bytes(mpad);  // multiple of 1024
-    const uint32_t a_box_bytes = static_cast<uint32_t>(mpad) * 64 * 2;
-    const int STAGES = T_::stages(mpad);
+    const uint32_t a_stage_bytes = static_cast<uint32_t>(mpad) * BK * 2;  // multiple of 1024
+    const int STAGES = stages_for(mpad);
     uint8_t *sB = smem;
     uint8_t *sA = smem + STAGES * B_STAGE_BYTES;
     uint64_t *bars = reinterpret_cast<uint64_t *>(sA + STAGES * a_stage_bytes);
@@ -124,9 +97,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     volatile int *last_flag = abort_flag + 1;
 
     const uint32_t warp = warp_id(), lane = lane_id();
-    const int n_tiles = (N + TN - 1) / TN;
-    const int num_ku = (K + KU - 1) / KU;
-    const long long T = static_cast<long long>(n_tiles) * num_ku;
+    const int n_tiles = (N + BN_T - 1) / BN_T;
+    const int num_kb = (K + BK - 1) / BK;
+    const long long T = static_cast<long long>(n_tiles) * num_kb;
     const int G = static_cast<int>(gridDim.x);
     const int c = static_cast<int>(blockIdx.x);
     const long long r0 = range_start(c, T, G), r1 = range_start(c + 1, T, G);
@@ -159,26 +132,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     // (it takes an SM when one of these CTAs exits).
     if (threadIdx.x == 0) grid_launch_dependents();
 
-    // The loads of unit x into ring stage s: B (16 KB) and this M's A boxes.
-    // TN = 128: two 64 n x 64 k boxes side by side (a box wholly beyond N is
-    // skipped); TN = 64: one 64 n x 128 k box.
-    auto b_bytes = [&](int n0) -> uint32_t {
-        return TN == 128 ? ((n0 + 64 < N) ? 2u : 1u) * B_BOX_BYTES : B_STAGE_BYTES;
-    };
-    auto load_b = [&](int s, int n0, int k0, uint64_t pol) {
-        if (TN == 128) {
-            tma_load_2d(sB + s * B_STAGE_BYTES, &tmB, &full[s], n0, k0, pol);
-            if (n0 + 64 < N) tma_load_2d(sB + s * B_STAGE_BYTES + B_BOX_BYTES, &tmB, &full[s], n0 + 64, k0, pol);
-        } else {
-            tma_load_2d(sB + s * B_STAGE_BYTES, &tmB, &full[s], n0, k0, pol);
-        }
-    };
-    auto load_a = [&](int s, int k0, uint64_t pol) {
-#pragma unroll
-        for (int j = 0; j < T_::A_BOXES; ++j)
-            tma_load_2d(sA + s * a_stage_bytes + j * a_box_bytes, &tmA, &full[s], k0 + 64 * j, 0, pol);
-    };
-
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
@@ -193,14 +146,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // dependency wait, A and the rest after it.
                 const long long pre_end = min(r1, r0 + static_cast<long long>(STAGES));
                 for (long long y = r0; y < pre_end; ++y) {
-                    const int t = static_cast<int>(y / num_ku), ku = static_cast<int>(y % num_ku);
-                    const int n0 = t * TN, s_ = static_cast<int>(y - r0);
-                    mbar_arrive_expect_tx(&full[s_], b_bytes(n0) + a_stage_bytes);
-                    load_b(s_, n0, ku * KU, policy_b);
+                    const int t = static_cast<int>(y / num_kb), kb = static_cast<int>(y % num_kb);
+                    const int n0 = t * BN_T, k0 = kb * BK, s_ = static_cast<int>(y - r0);
+                    const int nb = (n0 + 64 < N) ? 2 : 1;
+                    mbar_arrive_expect_tx(&full[s_], nb * B_BOX_BYTES + a_stage_bytes);
+                    for (int j = 0; j < nb; ++j)
+                        tma_load_2d(sB + s_ * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB, &full[s_],
+                                    n0 + 64 * j, k0, policy_b);
                 }
                 grid_dependency_wait();
-                for (long long y = r0; y < pre_end; ++y)
-                    load_a(static_cast<int>(y - r0), static_cast<int>(y % num_ku) * KU, policy_a);
+                for (long long y = r0; y < pre_end; ++y) {
+                    const int s_ = static_cast<int>(y - r0);
+                    tma_load_2d(sA + s_ * a_stage_bytes, &tmA, &full[s_],
+                                static_cast<int>(y % num_kb) * BK, 0, policy_a);
+                }
                 issued = static_cast<uint32_t>(pre_end - r0);
                 stage = issued % static_cast<uint32_t>(STAGES);
                 phase = (issued == static_cast<uint32_t>(STAGES)) ? 1u : 0u;
@@ -209,15 +168,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                 grid_dependency_wait();
             }
             for (; x < r1 && ok; ++x) {
-                const int t = static_cast<int>(x / num_ku), ku = static_cast<int>(x % num_ku);
-                const int n0 = t * TN, k0 = ku * KU;
+                const int t = static_cast<int>(x / num_kb), kb = static_cast<int>(x % num_kb);
+                const int n0 = t * BN_T, k0 = kb * BK;
+                const int nb = (n0 + 64 < N) ? 2 : 1;  // skip a box wholly beyond N
                 if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, kSiteProducerEmpty)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&full[stage], b_bytes(n0) + a_stage_bytes);
-                load_b(static_cast<int>(stage), n0, k0, policy_b);
-                load_a(static_cast<int>(stage), k0, policy_a);
+                mbar_arrive_expect_tx(&full[stage], nb * B_BOX_BYTES + a_stage_bytes);
+                for (int j = 0; j < nb; ++j)
+                    tma_load_2d(sB + stage * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB, &full[stage],
+                                n0 + 64 * j, k0, policy_b);
+                tma_load_2d(sA + stage * a_stage_bytes, &tmA, &full[stage], k0, 0, policy_a);
                 ++issued;
                 if (++stage == STAGES) {
                     stage = 0;
@@ -240,13 +202,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             // The bounded waits below time this launch's own pipeline, not
             // the preceding kernel (A arrives only after that wait anyway).
             grid_dependency_wait();
-            const uint32_t idesc = idesc_f16_f32(TN, static_cast<uint32_t>(mpad), true, false);
+            const uint32_t idesc = idesc_f16_f32(BN_T, static_cast<uint32_t>(mpad), true, false);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true, issued_any = false;
             long long x = r0;
             while (x < r1 && ok) {
-                const int t = static_cast<int>(x / num_ku);
-                const long long seg_end = min(r1, static_cast<long long>(t + 1) * num_ku);
+                const int t = static_cast<int>(x / num_kb);
+                const long long seg_end = min(r1, static_cast<long long>(t + 1) * num_kb);
                 if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, status, kSiteMmaAccEmpty)) {
                     ok = false;
                     break;
@@ -263,13 +225,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
                     const uint32_t a_base = smem_u32(sA + stage * a_stage_bytes);
 #pragma unroll
-                    for (int kk = 0; kk < KU / 16; ++kk) {
-                        // B^T: MN-major rows of 128 B (64 n), 16 k rows per step;
-                        // for TN = 128 the second 64-n block is 8 KB on.
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        // B^T: MN-major, n-blocks 8 KB apart, k groups 1 KB apart.
                         const uint64_t b_desc = smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
-                        // A^T: K-major rows of 128 B (one per m), one box per 64 k.
-                        const uint64_t a_desc =
-                            smem_desc_sw128(a_base + (kk / 4) * a_box_bytes + (kk % 4) * 32, 16, 1024);
+                        // A^T: K-major rows of 128 B (one per m).
+                        const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
                         umma_f16_ss(d_tmem, b_desc, a_desc, idesc, (first && kk == 0) ? 0u : 1u);
                     }
                     first = false;
@@ -296,22 +256,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---------------- epilogue and fix-up (warps 2..5) ----------------
         grid_dependency_wait();  // C and the workspace may be the preceding kernel's
         const uint32_t q = warp & 3u;
-        // Accumulator row i (n within the tile) sits in TMEM lane i for
-        // TN = 128; for TN = 64 (MMA M = 64) rows 16 j .. 16 j + 15 sit in
-        // lanes 32 j .. 32 j + 15, so lanes 16..31 of each warp hold nothing.
-        const bool active = TN == 128 || lane < 16;
-        const int nl = TN == 128 ? static_cast<int>(q * 32 + lane) : static_cast<int>(q * 16 + (lane & 15u));
+        const int nl = static_cast<int>(q * 32 + lane);  // n within the tile
         const bool leader = (warp == 2 && lane == 0);
         uint32_t acc = 0, acc_phase = 0;
         long long x = r0;
         while (x < r1) {
-            const int t = static_cast<int>(x / num_ku);
-            const long long tile_lo = static_cast<long long>(t) * num_ku, tile_hi = tile_lo + num_ku;
+            const int t = static_cast<int>(x / num_kb);
+            const long long tile_lo = static_cast<long long>(t) * num_kb, tile_hi = tile_lo + num_kb;
             const long long seg_end = min(r1, tile_hi);
             const bool whole = (x == tile_lo && seg_end == tile_hi);
             const int slot = (x == r0) ? 0 : 1;  // a partial segment is the range's first or last
             x = seg_end;
-            const int n = active ? t * TN + nl : N;  // N: this thread touches no column
+            const int n = t * BN_T + nl;
             // The four warps decide together whether to go on: a warp that
             // gave up has raised the abort flag before this barrier.
             const bool ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull);
@@ -353,15 +309,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 named_bar_sync(1, 128);
                 bool last = *last_flag != 0;
                 if (!last) {
-                    float *part = partials + (static_cast<size_t>(c) * 2 + slot) * TN * mpad;
+                    float *part = partials + (static_cast<size_t>(c) * 2 + slot) * BN_T * mpad;
                     for (int j = 0; j < chunks; ++j) {
                         uint32_t r[16];
                         tmem_ld_32x32b_x16(t_row + 16 * j, r);
                         tmem_ld_wait();
-                        if (active) {
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) part[(16 * j + i) * TN + nl] = __uint_as_float(r[i]);
-                        }
+                        for (int i = 0; i < 16; ++i) part[(16 * j + i) * BN_T + nl] = __uint_as_float(r[i]);
                     }
                     __threadfence();
                     named_bar_sync(1, 128);
@@ -395,11 +349,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                                     const int cc = cb + k;
                                     if (cc > c_hi || cc == c) continue;
                                     const long long s_cc = range_start(cc, T, G);
-                                    const int sl = (s_cc / num_ku == t) ? 0 : 1;
-                                    const float *pc = partials + (static_cast<size_t>(cc) * 2 + sl) * TN * mpad;
+                                    const int sl = (s_cc / num_kb == t) ? 0 : 1;
+                                    const float *pc = partials + (static_cast<size_t>(cc) * 2 + sl) * BN_T * mpad;
 #pragma unroll
                                     for (int i = 0; i < 16; ++i)
-                                        pv[k][i] = (16 * j + i < M) ? __ldcg(pc + (16 * j + i) * TN + nl) : 0.f;
+                                        pv[k][i] = (16 * j + i < M) ? __ldcg(pc + (16 * j + i) * BN_T + nl) : 0.f;
                                 }
 #pragma unroll
                                 for (int k = 0; k < 4; ++k) {
@@ -436,13 +390,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-// The tile width for a call: 64-column tiles when the 128-column ones are
-// fewer than the CTAs (so some ranges would lie inside one tile) and M is
-// small enough that re-reading A once per 64 columns costs little.
-inline int tile_width(int M, int N, int sm_count) {
-    return (M <= 64 && (N + 127) / 128 < sm_count && (N + 63) / 64 >= sm_count) ? 64 : 128;
-}
-
 }  // namespace skinny
 
 namespace {
@@ -458,17 +405,7 @@ Workspace g_ws[64];
 // Tile counters, then two partial slots (128 x M fp32) per CTA for up to 160
 // CTAs at M = 128: 21.25 MB.
 constexpr size_t kWorkspaceBytes =
-    skinny::COUNTER_BYTES + 160u * 2u * skinny::Tile<128>::slot_bytes(skinny::MAX_M);
-
-// Raises both kernels' dynamic shared memory limit on the current device.
-cudaError_t skinny_set_attributes() {
-    cudaError_t e = cudaFuncSetAttribute(skinny::gemm_skinny_kernel<128>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(skinny::SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(skinny::gemm_skinny_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(skinny::SMEM_BYTES));
-}
+    skinny::COUNTER_BYTES + 160u * 2u * skinny::BN_T * skinny::MAX_M * sizeof(float);
 
 // The library's per-device workspace of the skinny kernel (tile counters +
 // partial slots), allocated and zeroed on the first call on a device.
@@ -492,7 +429,8 @@ int workspace(Workspace **out) {
         w.bytes = kWorkspaceBytes;
     }
     if (!w.attr_set) {
-        e = skinny_set_attributes();
+        e = cudaFuncSetAttribute(skinny::gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(skinny::SMEM_BYTES));
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(skinny)");
         w.attr_set = true;
     }
@@ -502,19 +440,17 @@ int workspace(Workspace **out) {
 
 }  // namespace
 
-// Launches the few-row kernel with tile width TN.  pdl > 0 adds programmatic
-// stream serialization: the kernel may be launched while the preceding kernel
-// in the stream finishes, and waits on it (griddepcontrol.wait) before it
-// reads A, C or the workspace; pdl == 2 also lets it request B before that
-// wait.
-template <int TN>
-cudaError_t launch_skinny(int grid, cudaStream_t stream, int pdl, const CUtensorMap &tmB, const CUtensorMap &tmA,
-                          float *c, int M, int N, int K, long long ldc, int mpad, unsigned int *counters,
-                          float *partials, unsigned int *status) {
+// Launches the few-row kernel.  pdl > 0 adds programmatic stream
+// serialization: the kernel may be launched while the preceding kernel in the
+// stream finishes, and waits on it (griddepcontrol.wait) before it reads A, C
+// or the workspace; pdl == 2 also lets it request B before that wait.
+cudaError_t launch_skinny(int grid, size_t smem, cudaStream_t stream, int pdl, const CUtensorMap &tmB,
+                          const CUtensorMap &tmA, float *c, int M, int N, int K, long long ldc, int mpad,
+                          unsigned int *counters, float *partials, unsigned int *status) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
     cfg.blockDim = dim3(skinny::THREADS, 1, 1);
-    cfg.dynamicSmemBytes = skinny::Tile<TN>::smem(mpad);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     if (pdl > 0) {
@@ -523,30 +459,8 @@ cudaError_t launch_skinny(int grid, cudaStream_t stream, int pdl, const CUtensor
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, skinny::gemm_skinny_kernel<TN>, tmB, tmA, c, M, N, K, ldc, mpad, counters,
+    return cudaLaunchKernelEx(&cfg, skinny::gemm_skinny_kernel, tmB, tmA, c, M, N, K, ldc, mpad, counters,
                               partials, status, pdl == 2 ? 1 : 0);
-}
-
-// The tensor maps of the few-row kernel: B (K x N fp16, row pitch ldb) in
-// boxes of 64 n x (64 or 128) k, A (M x K fp16, row pitch lda) in boxes of
-// 64 k x mpad rows, both with 128-byte swizzle.
-int skinny_maps(int tn, const void *a, const void *b, int M, int N, int K, int64_t lda, int64_t ldb, int mpad,
-                CUtensorMap *tmB, CUtensorMap *tmA) {
-    {
-        const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
-        const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
-        const uint32_t box[2] = {64, static_cast<uint32_t>(tn == 64 ? 128 : 64)};
-        int rc = encode_tiled_internal(tmB, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(b), dims,
-                                       strides, box, nullptr, CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B,
-                                       CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
-        if (rc != CUDAIR_OK) return rc;
-    }
-    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
-    const uint32_t box[2] = {64, static_cast<uint32_t>(mpad)};
-    return encode_tiled_internal(tmA, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(a), dims, strides,
-                                 box, nullptr, CUDAIR_INTERLEAVE_NONE, CUDAIR_SWIZZLE_128B,
-                                 CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
 }
 
 // Called after a bounded wait gave up: a launch that unwound early may have
@@ -569,8 +483,7 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
     if (M < 1 || M > skinny::MAX_M)
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: the few-row kernel takes 1 <= M <= %d, got %d",
                          skinny::MAX_M, M);
-    const int tn = skinny::tile_width(M, N, sm_count);
-    const int n_tiles = (N + tn - 1) / tn;
+    const int n_tiles = (N + skinny::BN_T - 1) / skinny::BN_T;
     if (n_tiles > skinny::MAX_TILES)
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: N = %d too large for the few-row kernel", N);
     Workspace *ws = nullptr;
@@ -579,22 +492,35 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
     const int mpad = (M + 15) / 16 * 16;
 
     alignas(64) CUtensorMap tmB, tmA;
-    if ((rc = skinny_maps(tn, a, b, M, N, K, lda, ldb, mpad, &tmB, &tmA)) != CUDAIR_OK) return rc;
-    const int ku = tn == 64 ? skinny::Tile<64>::KU : skinny::Tile<128>::KU;
-    const long long T = static_cast<long long>(n_tiles) * ((K + ku - 1) / ku);
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+        const uint32_t box[2] = {64, skinny::BK};
+        rc = encode_tiled_internal(&tmB, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(b),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+        const uint32_t box[2] = {skinny::BK, static_cast<uint32_t>(mpad)};
+        rc = encode_tiled_internal(&tmA, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(a),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    const long long T = static_cast<long long>(n_tiles) * ((K + skinny::BK - 1) / skinny::BK);
     // One CTA per SM, as many as there are units and as the partial slots hold.
-    const size_t slot = tn == 64 ? skinny::Tile<64>::slot_bytes(mpad) : skinny::Tile<128>::slot_bytes(mpad);
-    const long long slots_fit = static_cast<long long>((ws->bytes - skinny::COUNTER_BYTES) / (2 * slot));
+    const long long slots_fit = static_cast<long long>(ws->bytes - skinny::COUNTER_BYTES) /
+                                (2LL * skinny::BN_T * mpad * static_cast<long long>(sizeof(float)));
     long long g = T < sm_count ? T : sm_count;
     if (g > slots_fit) g = slots_fit;
     const int grid = static_cast<int>(g);
     unsigned int *counters = static_cast<unsigned int *>(ws->ptr);
     float *partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws->ptr) + skinny::COUNTER_BYTES);
-    const cudaError_t e =
-        tn == 64 ? launch_skinny<64>(grid, stream, gemm_pdl_mode(), tmB, tmA, c, M, N, K,
-                                     static_cast<long long>(ldc), mpad, counters, partials, status)
-                 : launch_skinny<128>(grid, stream, gemm_pdl_mode(), tmB, tmA, c, M, N, K,
-                                      static_cast<long long>(ldc), mpad, counters, partials, status);
+    cudaError_t e = launch_skinny(grid, skinny::smem_for(mpad), stream, gemm_pdl_mode(), tmB, tmA, c, M, N,
+                                  K, static_cast<long long>(ldc), mpad, counters, partials, status);
     if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch");
     return CUDAIR_OK;
 }
@@ -664,7 +590,7 @@ int noalloc_scratch(unsigned char **out) {
         g_noalloc_ptr[dev] = static_cast<unsigned char *>(p);
     }
     if (!g_noalloc_attr[dev]) {
-        e = cudaFuncSetAttribute(skinny::gemm_skinny_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(skinny::gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(skinny::SMEM_BYTES));
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(skinny)");
         g_noalloc_attr[dev] = true;
@@ -700,10 +626,10 @@ CUDAIR_API int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm_noalloc: M = %lld exceeds the maximum of %d rows", (long long)M,
                          kNoAllocMaxM);
-    if (N > static_cast<int64_t>(kNoAllocMaxTiles) * 128)
+    if (N > static_cast<int64_t>(kNoAllocMaxTiles) * skinny::BN_T)
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm_noalloc: N = %lld exceeds the maximum of %d columns", (long long)N,
-                         kNoAllocMaxTiles * 128);
+                         kNoAllocMaxTiles * skinny::BN_T);
     if (K > INT32_MAX)
         return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_noalloc: K must fit int32");
     if (!a || !b || !c) return set_error(CUDAIR_ERR_INVALID, "cudair: gemm_noalloc: nil pointer");
@@ -731,10 +657,27 @@ CUDAIR_API int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c
     const int Mi = static_cast<int>(M), Ni = static_cast<int>(N), Ki = static_cast<int>(K);
     const int mpad = (Mi + 15) / 16 * 16;
     alignas(64) CUtensorMap tmB, tmA;
-    if ((rc = skinny_maps(128, a, b, Mi, Ni, Ki, lda, ldb, mpad, &tmB, &tmA)) != CUDAIR_OK) return rc;
-    const int n_tiles = (Ni + 127) / 128;
-    const long long T = static_cast<long long>(n_tiles) * ((Ki + skinny::Tile<128>::KU - 1) / skinny::Tile<128>::KU);
-    const long long slot_pair = 2LL * static_cast<long long>(skinny::Tile<128>::slot_bytes(mpad));
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+        const uint32_t box[2] = {64, skinny::BK};
+        rc = encode_tiled_internal(&tmB, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(b),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+        const uint32_t box[2] = {skinny::BK, static_cast<uint32_t>(mpad)};
+        rc = encode_tiled_internal(&tmA, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(a),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    const int n_tiles = (Ni + skinny::BN_T - 1) / skinny::BN_T;
+    const long long T = static_cast<long long>(n_tiles) * ((Ki + skinny::BK - 1) / skinny::BK);
+    const long long slot_pair = 2LL * skinny::BN_T * mpad * static_cast<long long>(sizeof(float));
     long long grid = T < sms ? T : sms;
     const long long fit = static_cast<long long>(kNoAllocPartialBytes) / slot_pair;
     if (grid > fit) grid = fit;
@@ -744,7 +687,7 @@ CUDAIR_API int cudair_gemm_f16f32_noalloc(const void *a, const void *b, float *c
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaMemsetAsync(counters, 0, static_cast<size_t>(n_tiles) * sizeof(unsigned int), s);
     if (e != cudaSuccess) return cuda_error(e, "cudaMemsetAsync(no-alloc tile counters)");
-    skinny::gemm_skinny_kernel<128><<<static_cast<unsigned>(grid), skinny::THREADS, skinny::Tile<128>::smem(mpad), s>>>(
+    skinny::gemm_skinny_kernel<<<static_cast<unsigned>(grid), skinny::THREADS, skinny::smem_for(mpad), s>>>(
         tmB, tmA, c, Mi, Ni, Ki, static_cast<long long>(ldc), mpad, counters, partials, status, 0);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch (no-alloc)");

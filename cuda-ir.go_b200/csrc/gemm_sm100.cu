@@ -1018,14 +1018,16 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
     // fewer it leaves SMs idle and pays its fix-up anyway (128^3: 14.1 us
     // against 5.3 us for the single-CTA kernel).
     const int64_t units = ((N + 127) / 128) * ((K + 63) / 64);
-    const bool fewrows_auto = variant == 0 && flags == 0 && (M <= 64 || (M <= 128 && N <= 8192)) &&
-                              units >= dev->sm_count;
     // A problem of one wave of the small-problem kernel's 128 x 64 tiles
     // with K <= 512 takes that kernel: the whole K panel is loaded at once,
-    // and the pipelined kernels' set-up would not be amortised.
+    // and neither the pipelined kernels' set-up nor the few-row kernel's
+    // split-K fix-up is amortised at that size (128 x 4096 x 512: 5.9 us,
+    // against 26.6 us for the few-row kernel and 9.4 us for CTA pairs).
     const int64_t small_tiles = ((M + 127) / 128) * ((N + 63) / 64);
-    const bool small_auto = variant == 0 && flags == 0 && !fewrows_auto && K <= 64 * kSmallMaxKBlocks &&
+    const bool small_auto = variant == 0 && flags == 0 && K <= 64 * kSmallMaxKBlocks &&
                             small_tiles <= dev->sm_count;
+    const bool fewrows_auto = variant == 0 && flags == 0 && !small_auto && (M <= 64 || (M <= 128 && N <= 8192)) &&
+                              units >= dev->sm_count;
     const int use_variant = small_auto ? 5 : variant;
     if (variant == 3 || fewrows_auto)
         return gemm_skinny_launch(a, b, static_cast<float *>(c), static_cast<int>(M), static_cast<int>(N),

@@ -377,13 +377,13 @@ def test_fewrows_contributors_per_tile(dev, cudair, M, kb):
 
 @pytest.mark.parametrize("M", [1, 5, 16, 40, 64])
 @pytest.mark.parametrize("N,K", [(14336, 4096), (9416, 1000), (18816, 136), (12000, 64), (10000, 4104)])
-def test_fewrows_64_column_tiles(dev, cudair, M, N, K):
-    # Shapes with fewer 128-column tiles than SMs but at least as many
-    # 64-column ones take the few-row kernel's 64-column tiles (MMA M = 64,
-    # 128-wide k units): the decode shape, exactly one tile per CTA
-    # (N = 9416), ragged N and K (a k unit half or wholly beyond K), K under
-    # one unit.  Exact (integer data), twice in a row from the same C
-    # (bit-identical), and C's padding columns untouched.
+def test_fewrows_fewer_tiles_than_sms(dev, cudair, M, N, K):
+    # The few-row kernel on shapes with fewer 128-column tiles than SMs, so
+    # that some CTAs' ranges lie inside one tile and a tile can have two
+    # contributors finishing together: the decode shape, ragged N and K, K of
+    # a single k-block, N with 74 to 147 tiles.  Exact (integer data), twice
+    # in a row from the same C (bit-identical), and C's padding columns
+    # untouched.
     import torch
     from cudair import kernels
     kernels.set_gemm_variant(3)
