@@ -47,12 +47,6 @@ constexpr uint32_t B_BOX_BYTES = 64 * BK * 2;        // 64 n x 64 k
 constexpr uint32_t B_STAGE_BYTES = 2 * B_BOX_BYTES;  // 16 KB
 constexpr uint32_t BAR_BYTES = 256;
 constexpr size_t SMEM_BYTES = 227 * 1024;  // the launch's dynamic shared memory limit
-// Units of B beyond the ring that a launch with B requested early also
-// prefetches into L2 before its dependency wait (16: 256 KB per CTA).
-#ifndef CUDAIR_SKINNY_PREFETCH_UNITS
-#define CUDAIR_SKINNY_PREFETCH_UNITS 16
-#endif
-constexpr int kPrefetchUnits = CUDAIR_SKINNY_PREFETCH_UNITS;
 
 // The ring holds as many stages of (B tile + this M's A tile) as fit: with
 // M <= 16 that is 12 stages (192 KB of B in flight per SM), with M = 64 nine,
@@ -159,16 +153,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int j = 0; j < nb; ++j)
                         tma_load_2d(sB + s_ * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB, &full[s_],
                                     n0 + 64 * j, k0, policy_b);
-                }
-                // While the preceding kernel finishes, HBM has room: the
-                // units after the ring are requested into L2 as well, so
-                // after the wait they load from there.
-                const long long pf_end = min(r1, pre_end + static_cast<long long>(kPrefetchUnits));
-                for (long long y = pre_end; y < pf_end; ++y) {
-                    const int t = static_cast<int>(y / num_kb), kb = static_cast<int>(y % num_kb);
-                    const int n0 = t * BN_T, k0 = kb * BK;
-                    tma_prefetch_l2_2d(&tmB, n0, k0, policy_b);
-                    if (n0 + 64 < N) tma_prefetch_l2_2d(&tmB, n0 + 64, k0, policy_b);
                 }
                 grid_dependency_wait();
                 for (long long y = r0; y < pre_end; ++y) {

@@ -116,18 +116,6 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
-// 2D tile prefetch global -> L2 (no shared memory, nothing to wait for): the
-// box's lines are requested into L2 so that a later load of the same box hits
-// there.  The coordinate rules are those of the load above.
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int32_t x, int32_t y,
-                                                   uint64_t cache_hint) {
-    asm volatile(
-        "cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
-            reinterpret_cast<uint64_t>(map)),
-        "r"(x), "r"(y), "l"(cache_hint)
-        : "memory");
-}
-
 // 2D tile reduce-add shared -> global: L2 adds the box element-wise into the
 // tensor (fp32 add, round to nearest); elements outside the tensor are
 // skipped.  x (innermost) * element size must be a multiple of 16 bytes and
