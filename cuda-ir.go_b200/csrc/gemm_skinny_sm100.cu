@@ -268,22 +268,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int slot = (x == r0) ? 0 : 1;  // a partial segment is the range's first or last
             x = seg_end;
             const int n = t * BN_T + nl;
-            // A partial tile's contributors c_lo .. c_hi.  When there are
-            // exactly two, the tile's head is the last segment of c_lo's range
-            // and its tail the first of c_hi's, so c_lo is the one expected to
-            // finish the tile: it reads the tile's counter now, while this
-            // segment's last MMAs run.  With three or more, the lower two both
-            // end their ranges here and neither can expect the other's part.
-            int c_lo = 0, c_hi = 0;
-            unsigned int others = 0, early = ~0u;
-            bool try_last = false;
-            if (!whole) {
-                c_lo = cta_of(tile_lo, T, G);
-                c_hi = cta_of(tile_hi - 1, T, G);
-                others = static_cast<unsigned int>(c_hi - c_lo);
-                try_last = (c == c_lo && others == 1u);
-                if (try_last && leader) early = ld_acquire_gpu_u32(&counters[t]);
-            }
             // The four warps decide together whether to go on: a warp that
             // gave up has raised the abort flag before this barrier.
             const bool ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull);
@@ -318,11 +302,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // the tile counter.  Each other contributor writes its part to
                 // the workspace, makes it visible and counts itself in.  A
                 // contributor that finds all the others counted in already is
-                // last without writing its part (only the expected finisher
-                // looks: for the others the check would cost a memory round
-                // trip and seldom succeed).
-                if (leader)
-                    *last_flag = (try_last && (early == others || ld_acquire_gpu_u32(&counters[t]) == others)) ? 1 : 0;
+                // last without writing its part.
+                const int c_lo = cta_of(tile_lo, T, G), c_hi = cta_of(tile_hi - 1, T, G);
+                const unsigned int others = static_cast<unsigned int>(c_hi - c_lo);
+                if (leader) *last_flag = (ld_acquire_gpu_u32(&counters[t]) == others) ? 1 : 0;
                 named_bar_sync(1, 128);
                 bool last = *last_flag != 0;
                 if (!last) {
