@@ -268,11 +268,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int slot = (x == r0) ? 0 : 1;  // a partial segment is the range's first or last
             x = seg_end;
             const int n = t * BN_T + nl;
-            // The four warps decide together whether to go on (a barrier that
-            // ORs every thread's answer: the abort flag may be raised by
-            // another role while they read it).
+            // The four warps decide together whether to go on: a warp that
+            // gave up has raised the abort flag before this barrier.
             const bool ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull);
-            if (named_bar_or(1, 128, !ok || *abort_flag != 0)) break;
+            named_bar_sync(1, 128);
+            if (!ok || *abort_flag) break;
             tc_fence_after_sync();
             // This thread's column of the accumulator, read from TMEM sixteen
             // rows at a time wherever it is needed; the accumulator is handed
@@ -390,406 +390,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-// =============================================================================
-// The same GEMM for M <= 16 on clusters of two CTAs, for shapes with fewer
-// 128-column tiles than SMs (the decode shape: 112 tiles on 148 SMs).
-//
-// With one stream-K range per CTA, a range is shorter than a tile there, so
-// some ranges lie inside one tile, and such a tile ends up with two
-// contributors whose parts are both finished at the end of the launch: their
-// hand-over (publish, count, read) is chained onto the launch's tail.  Here
-// the ranges belong to clusters (74 of them, each longer than a tile), so
-// every range crosses a tile boundary and every tile shared between two
-// ranges is the last segment of one (finished late) and the first of the
-// other (published early).  Inside a cluster, each segment's 64-wide k-blocks
-// are split between the two CTAs, the even one taking the first half; each
-// accumulates its half in its own TMEM, the odd CTA hands its 128 x 16 fp32
-// part to the even one through distributed shared memory, and the even CTA
-// adds the two (even + odd, a fixed order) and does the segment's epilogue
-// and fix-up exactly as gemm_skinny_kernel does, with clusters in place of
-// CTAs.  B is still read 256 bytes per k-row (two 64 x 64 boxes side by side).
-// =============================================================================
-
-constexpr uint32_t XBUF_BYTES = BN_T * 16 * sizeof(float);  // the odd CTA's part, 8 KB
-constexpr uint32_t PAIR_BAR_BYTES = 512;
-__host__ __device__ constexpr int pair_stages() {
-    return static_cast<int>((SMEM_BYTES - 1024 - PAIR_BAR_BYTES - XBUF_BYTES) / (B_STAGE_BYTES + 16 * BK * 2)) <
-                   MAX_STAGES
-               ? static_cast<int>((SMEM_BYTES - 1024 - PAIR_BAR_BYTES - XBUF_BYTES) / (B_STAGE_BYTES + 16 * BK * 2))
-               : MAX_STAGES;
-}
-__host__ __device__ constexpr size_t pair_smem() {
-    return 1024 + static_cast<size_t>(pair_stages()) * (B_STAGE_BYTES + 16 * BK * 2) + XBUF_BYTES + PAIR_BAR_BYTES;
-}
-static_assert(pair_smem() <= SMEM_BYTES, "shared memory budget");
-static_assert(2 * MAX_STAGES * 8 + 7 * 8 + 12 <= PAIR_BAR_BYTES, "barrier area");
-
-// The part of the segment that starts at unit x (a cluster range ends at r1)
-// that CTA `rank` of the cluster computes: [lo, hi), and the segment's end.
-struct Share {
-    long long lo, hi, seg_hi;
-};
-__device__ __forceinline__ Share share_of(long long x, long long r1, int num_kb, uint32_t rank) {
-    const long long t = x / num_kb;
-    const long long seg_hi = min(r1, (t + 1) * static_cast<long long>(num_kb));
-    const long long mid = x + (seg_hi - x + 1) / 2;
-    return rank == 0 ? Share{x, mid, seg_hi} : Share{mid, seg_hi, seg_hi};
-}
-
-__global__ void __launch_bounds__(THREADS, 1)
-    gemm_skinny_pair_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA,
-                            float *__restrict__ C, int M, int N, int K, long long ldc,
-                            unsigned int *__restrict__ counters, float *__restrict__ partials,
-                            unsigned int *status, int b_early) {
-    constexpr int MPAD = 16;
-    constexpr uint32_t a_stage_bytes = MPAD * BK * 2;  // 2 KB
-    constexpr int STAGES = pair_stages();
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t raw_addr = smem_u32(smem_raw);
-    uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);  // same offset in both CTAs
-
-    uint8_t *sB = smem;
-    uint8_t *sA = smem + STAGES * B_STAGE_BYTES;
-    float *xbuf = reinterpret_cast<float *>(sA + STAGES * a_stage_bytes);  // even CTA: the odd CTA's part
-    uint64_t *bars = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(xbuf) + XBUF_BYTES);
-    uint64_t *full = bars;
-    uint64_t *empty = bars + STAGES;
-    uint64_t *acc_full = bars + 2 * STAGES;
-    uint64_t *acc_empty = acc_full + 2;
-    uint64_t *drain = acc_empty + 2;
-    uint64_t *xfull = drain + 1;  // even CTA: the odd part landed (128 arrivals)
-    uint64_t *xfree = xfull + 1;  // odd CTA: the even CTA has read the last part (1 arrival)
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xfree + 1);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    volatile int *last_flag = abort_flag + 1;
-
-    const uint32_t warp = warp_id(), lane = lane_id();
-    const uint32_t rank = cluster_ctarank();  // 0: even CTA (epilogue of the cluster), 1: odd
-    const uint32_t peer = rank ^ 1u;
-    const int n_tiles = (N + BN_T - 1) / BN_T;
-    const int num_kb = (K + BK - 1) / BK;
-    const long long T = static_cast<long long>(n_tiles) * num_kb;
-    const int G = static_cast<int>(gridDim.x >> 1);  // clusters
-    const int u = static_cast<int>(blockIdx.x >> 1);
-    const long long r0 = range_start(u, T, G), r1 = range_start(u + 1, T, G);
-    constexpr uint32_t tmem_cols = 32;
-    const uint32_t peer_abort = mapa_shared(smem_u32(const_cast<int *>(abort_flag)), peer);
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);
-        }
-        mbar_init(drain, 1);
-        mbar_init(xfull, 128);
-        mbar_init(xfree, 1);
-        *abort_flag = 0;
-        fence_mbar_init();
-        tma_prefetch_map(&tmA);
-        tma_prefetch_map(&tmB);
-    }
-    if (warp == 1) {
-        tmem_alloc(tmem_slot, tmem_cols);
-        tmem_relinquish();
-    }
-    tc_fence_before_sync();
-    cluster_sync();  // both CTAs' barriers initialised before any remote arrive
-    tc_fence_after_sync();
-    const uint32_t tmem_base = *tmem_slot;
-    if (threadIdx.x == 0) grid_launch_dependents();
-    // A wait that gave up here also stops the other CTA of the cluster.
-    auto give_up = [&]() { st_shared_cluster_u32(peer_abort, 1u); };
-
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            const uint64_t policy_b = l2_policy_evict_normal();
-            const uint64_t policy_a = l2_policy_evict_last();
-            // This CTA's units in order: its share of each segment of the
-            // cluster's range.
-            long long wx = r0, w_cur = 0, w_hi = 0;
-            auto next_unit = [&](long long &unit) -> bool {
-                while (w_cur >= w_hi) {
-                    if (wx >= r1) return false;
-                    const Share s = share_of(wx, r1, num_kb, rank);
-                    w_cur = s.lo;
-                    w_hi = s.hi;
-                    wx = s.seg_hi;
-                }
-                unit = w_cur++;
-                return true;
-            };
-            auto load_b = [&](int s, long long unit) {
-                const int t = static_cast<int>(unit / num_kb), kb = static_cast<int>(unit % num_kb);
-                const int n0 = t * BN_T, k0 = kb * BK;
-                const int nb = (n0 + 64 < N) ? 2 : 1;
-                mbar_arrive_expect_tx(&full[s], nb * B_BOX_BYTES + a_stage_bytes);
-                for (int j = 0; j < nb; ++j)
-                    tma_load_2d(sB + s * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB, &full[s], n0 + 64 * j, k0,
-                                policy_b);
-            };
-            auto load_a = [&](int s, long long unit) {
-                tma_load_2d(sA + s * a_stage_bytes, &tmA, &full[s], static_cast<int>(unit % num_kb) * BK, 0,
-                            policy_a);
-            };
-            uint32_t stage = 0, phase = 0, issued = 0;
-            bool ok = true;
-            long long unit = 0;
-            if (b_early) {
-                // As in gemm_skinny_kernel: the first ring of B before the
-                // dependency wait, A after it.
-                long long pre_units[MAX_STAGES];
-                int pre = 0;
-                while (pre < STAGES && next_unit(unit)) {
-                    load_b(pre, unit);
-                    pre_units[pre++] = unit;
-                }
-                grid_dependency_wait();
-                for (int i = 0; i < pre; ++i) load_a(i, pre_units[i]);
-                issued = static_cast<uint32_t>(pre);
-                stage = issued % static_cast<uint32_t>(STAGES);
-                phase = (issued == static_cast<uint32_t>(STAGES)) ? 1u : 0u;
-            } else {
-                grid_dependency_wait();
-            }
-            while (ok && next_unit(unit)) {
-                if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, kSiteProducerEmpty)) {
-                    give_up();
-                    ok = false;
-                    break;
-                }
-                load_b(static_cast<int>(stage), unit);
-                load_a(static_cast<int>(stage), unit);
-                ++issued;
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
-            }
-            if (!ok) {
-                const uint32_t outstanding = issued < STAGES ? issued : STAGES;
-                for (uint32_t i = 1; i <= outstanding; ++i) {
-                    const uint32_t idx = issued - i;
-                    int never = 0;
-                    mbar_wait(&full[idx % STAGES], (idx / STAGES) & 1u, &never, status, kSiteDrain);
-                }
-            }
-        }
-        __syncwarp();
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            grid_dependency_wait();
-            const uint32_t idesc = idesc_f16_f32(BN_T, MPAD, true, false);
-            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
-            bool ok = true, issued_any = false;
-            long long x = r0;
-            while (x < r1 && ok) {
-                const Share sh = share_of(x, r1, num_kb, rank);
-                x = sh.seg_hi;
-                if (sh.lo == sh.hi) continue;  // the odd CTA's share of a one-unit segment
-                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, status, kSiteMmaAccEmpty)) {
-                    give_up();
-                    ok = false;
-                    break;
-                }
-                tc_fence_after_sync();
-                const uint32_t d_tmem = tmem_base + acc * MPAD;
-                for (long long y = sh.lo; y < sh.hi; ++y) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, status, kSiteMmaFull)) {
-                        give_up();
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after_sync();
-                    const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
-                    const uint32_t a_base = smem_u32(sA + stage * a_stage_bytes);
-#pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint64_t b_desc = smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
-                        const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
-                        umma_f16_ss(d_tmem, b_desc, a_desc, idesc, (y == sh.lo && kk == 0) ? 0u : 1u);
-                    }
-                    issued_any = true;
-                    umma_commit(&empty[stage]);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-                if (!ok) break;
-                umma_commit(&acc_full[acc]);
-                acc ^= 1u;
-                if (acc == 0) acc_phase ^= 1u;
-            }
-            if (!ok && issued_any) {
-                umma_commit(drain);
-                int never = 0;
-                mbar_wait(drain, 0, &never, status, kSiteDrain);
-            }
-        }
-        __syncwarp();
-    } else {
-        // ---------------- epilogue and fix-up (warps 2..5) ----------------
-        grid_dependency_wait();  // C and the workspace may be the preceding kernel's
-        const uint32_t q = warp & 3u;
-        const int nl = static_cast<int>(q * 32 + lane);  // n within the tile
-        const bool leader = (warp == 2 && lane == 0);
-        uint32_t acc = 0, acc_phase = 0, x_phase = 0;
-        const uint32_t xbuf_row = smem_u32(xbuf) + static_cast<uint32_t>(nl) * 64u;  // 16 floats per n
-        long long x = r0;
-        while (x < r1) {
-            const Share sh = share_of(x, r1, num_kb, rank);
-            const Share sh_odd = share_of(x, r1, num_kb, 1u);
-            const long long seg_lo = x;
-            x = sh.seg_hi;
-            const bool odd_part = sh_odd.lo < sh_odd.hi;
-            if (sh.lo == sh.hi) continue;  // the odd CTA has no part of this segment
-            // Every stop below is decided by all four warps together (a
-            // barrier that ORs their answers), so none is left at a later
-            // barrier; a wait that gave up also stops the other CTA.
-            const bool ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull);
-            if (!ok) give_up();
-            if (named_bar_or(1, 128, !ok || *abort_flag != 0)) break;
-            tc_fence_after_sync();
-            const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * MPAD;
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(t_row, r);
-            tmem_ld_wait();
-            if (rank == 1) {
-                // Hand the part to the even CTA once it has read the last one.
-                const bool free_ok = mbar_wait_cluster(xfree, x_phase ^ 1u, abort_flag, status, kSiteEpilogueAccFull);
-                if (!free_ok) give_up();
-                const bool stop = named_bar_or(1, 128, !free_ok || *abort_flag != 0);
-                if (!stop) {
-                    const uint32_t dst = mapa_shared(xbuf_row, 0);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        st_shared_cluster_v4(dst + 16u * j, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-                    mbar_arrive_cluster(mapa_shared(smem_u32(xfull), 0));
-                }
-                x_phase ^= 1u;
-                tc_fence_before_sync();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[acc]);
-                acc ^= 1u;
-                if (acc == 0) acc_phase ^= 1u;
-                if (stop) break;
-                continue;
-            }
-            // Even CTA: this segment's sum, its own part plus the odd CTA's.
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-            if (odd_part) {
-                const bool got = mbar_wait_cluster(xfull, x_phase, abort_flag, status, kSiteEpilogueAccFull);
-                if (!got) give_up();
-                if (named_bar_or(1, 128, !got || *abort_flag != 0)) break;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float4 o = *reinterpret_cast<const float4 *>(xbuf + nl * 16 + 4 * j);
-                    v[4 * j] += o.x;
-                    v[4 * j + 1] += o.y;
-                    v[4 * j + 2] += o.z;
-                    v[4 * j + 3] += o.w;
-                }
-                named_bar_sync(1, 128);  // every thread has read the part
-                if (leader) mbar_arrive_cluster(mapa_shared(smem_u32(xfree), 1));
-                x_phase ^= 1u;
-            }
-            const int t = static_cast<int>(seg_lo / num_kb);
-            const long long tile_lo = static_cast<long long>(t) * num_kb, tile_hi = tile_lo + num_kb;
-            const bool whole = (seg_lo == tile_lo && sh.seg_hi == tile_hi);
-            const int slot = (seg_lo == r0) ? 0 : 1;  // a partial segment is the range's first or last
-            const int n = t * BN_T + nl;
-            if (whole) {
-                if (n < N) {
-                    float cv[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) cv[i] = (i < M) ? C[static_cast<long long>(i) * ldc + n] : 0.f;
-#pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        if (i < M) C[static_cast<long long>(i) * ldc + n] = cv[i] + v[i];
-                }
-            } else {
-                // Partial tile, shared by clusters u_lo .. u_hi: the fix-up of
-                // gemm_skinny_kernel with clusters as the contributors.
-                const int u_lo = cta_of(tile_lo, T, G), u_hi = cta_of(tile_hi - 1, T, G);
-                const unsigned int others = static_cast<unsigned int>(u_hi - u_lo);
-                if (leader) *last_flag = (ld_acquire_gpu_u32(&counters[t]) == others) ? 1 : 0;
-                named_bar_sync(1, 128);
-                bool last = *last_flag != 0;
-                if (!last) {
-                    float *part = partials + (static_cast<size_t>(u) * 2 + slot) * BN_T * MPAD;
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) part[i * BN_T + nl] = v[i];
-                    __threadfence();
-                    named_bar_sync(1, 128);
-                    if (leader) {
-                        const unsigned int prev = atomicAdd(&counters[t], 1u);
-                        *last_flag = (prev == others) ? 1 : 0;
-                    }
-                    named_bar_sync(1, 128);
-                    last = *last_flag != 0;
-                }
-                if (last) {
-                    __threadfence();
-                    if (n < N) {
-                        float w[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) w[i] = (i < M) ? C[static_cast<long long>(i) * ldc + n] : 0.f;
-                        for (int ub = u_lo; ub <= u_hi; ub += 4) {
-                            float pv[4][16];
-#pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const int uu = ub + k;
-                                if (uu > u_hi || uu == u) continue;
-                                const long long s_uu = range_start(uu, T, G);
-                                const int sl = (s_uu / num_kb == t) ? 0 : 1;
-                                const float *pc = partials + (static_cast<size_t>(uu) * 2 + sl) * BN_T * MPAD;
-#pragma unroll
-                                for (int i = 0; i < 16; ++i) pv[k][i] = (i < M) ? __ldcg(pc + i * BN_T + nl) : 0.f;
-                            }
-#pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const int uu = ub + k;
-                                if (uu > u_hi) break;
-#pragma unroll
-                                for (int i = 0; i < 16; ++i) w[i] += (uu == u) ? v[i] : pv[k][i];
-                            }
-                        }
-#pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            if (i < M) C[static_cast<long long>(i) * ldc + n] = w[i];
-                    }
-                    if (leader) counters[t] = 0u;
-                }
-                named_bar_sync(1, 128);  // last_flag is reused by the next partial tile
-            }
-            tc_fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[acc]);
-            acc ^= 1u;
-            if (acc == 0) acc_phase ^= 1u;
-        }
-        __syncwarp();
-    }
-
-    // Neither CTA leaves (or frees TMEM) while the other may still write its
-    // shared memory: every remote store and arrive precedes this barrier.
-    tc_fence_before_sync();
-    __syncthreads();
-    cluster_sync();
-    if (warp == 1) {
-        tc_fence_after_sync();
-        tmem_dealloc(tmem_base, tmem_cols);
-    }
-}
-
 }  // namespace skinny
 
 namespace {
@@ -798,7 +398,6 @@ struct Workspace {
     void *ptr = nullptr;
     size_t bytes = 0;
     bool attr_set = false;
-    int pair_clusters = 0;  // clusters of the two-CTA kernel resident at once
 };
 std::mutex g_ws_mu;
 Workspace g_ws[64];
@@ -833,25 +432,6 @@ int workspace(Workspace **out) {
         e = cudaFuncSetAttribute(skinny::gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(skinny::SMEM_BYTES));
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(skinny)");
-        e = cudaFuncSetAttribute(skinny::gemm_skinny_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(skinny::SMEM_BYTES));
-        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(skinny pair)");
-        int sms = 0;
-        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return cuda_error(e, "cudaDeviceGetAttribute");
-        cudaLaunchConfig_t cfg = {};
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
-        cfg.blockDim = dim3(skinny::THREADS, 1, 1);
-        cfg.dynamicSmemBytes = skinny::pair_smem();
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        e = cudaOccupancyMaxActiveClusters(&w.pair_clusters, skinny::gemm_skinny_pair_kernel, &cfg);
-        if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveClusters(skinny pair)");
         w.attr_set = true;
     }
     *out = &w;
@@ -931,41 +511,14 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
         if (rc != CUDAIR_OK) return rc;
     }
     const long long T = static_cast<long long>(n_tiles) * ((K + skinny::BK - 1) / skinny::BK);
-    unsigned int *counters = static_cast<unsigned int *>(ws->ptr);
-    float *partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws->ptr) + skinny::COUNTER_BYTES);
-    // M <= 16 with fewer 128-column tiles than SMs: the two-CTA-cluster form,
-    // one cluster per two SMs (as many as are resident at once and as there
-    // are units).
-    if (mpad == 16 && n_tiles < sm_count && ws->pair_clusters >= 1) {
-        long long clusters = T < ws->pair_clusters ? T : ws->pair_clusters;
-        if (clusters > sm_count / 2) clusters = sm_count / 2;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
-        cfg.blockDim = dim3(skinny::THREADS, 1, 1);
-        cfg.dynamicSmemBytes = skinny::pair_smem();
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[2];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[1].val.programmaticStreamSerializationAllowed = 1;
-        const int pdl = gemm_pdl_mode();
-        cfg.attrs = attr;
-        cfg.numAttrs = pdl > 0 ? 2 : 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, skinny::gemm_skinny_pair_kernel, tmB, tmA, c, M, N, K,
-                                           static_cast<long long>(ldc), counters, partials, status,
-                                           pdl == 2 ? 1 : 0);
-        if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_pair_kernel launch");
-        return CUDAIR_OK;
-    }
     // One CTA per SM, as many as there are units and as the partial slots hold.
     const long long slots_fit = static_cast<long long>(ws->bytes - skinny::COUNTER_BYTES) /
                                 (2LL * skinny::BN_T * mpad * static_cast<long long>(sizeof(float)));
     long long g = T < sm_count ? T : sm_count;
     if (g > slots_fit) g = slots_fit;
     const int grid = static_cast<int>(g);
+    unsigned int *counters = static_cast<unsigned int *>(ws->ptr);
+    float *partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws->ptr) + skinny::COUNTER_BYTES);
     cudaError_t e = launch_skinny(grid, skinny::smem_for(mpad), stream, gemm_pdl_mode(), tmB, tmA, c, M, N,
                                   K, static_cast<long long>(ldc), mpad, counters, partials, status);
     if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch");

@@ -99,39 +99,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     }
 }
 
-// The same bounded wait with acquire semantics at cluster scope, for a
-// barrier that threads of another CTA of the cluster arrive on (with release
-// at cluster scope) after writing this CTA's shared memory.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                                  unsigned int *status, uint32_t site,
-                                                  uint64_t limit_ns = kWaitLimitNs) {
-    const uint32_t a = smem_u32(bar);
-    auto try_wait = [&]() -> bool {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(a), "r"(parity)
-            : "memory");
-        return ok != 0;
-    };
-    if (try_wait()) return true;
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t it = 1;; ++it) {
-        if (try_wait()) return true;
-        if ((it & 15u) == 0u) {
-            if (*abort) return false;
-            if (globaltimer_ns() - t0 > limit_ns) {
-                *abort = 1;
-                atomicOr(status, site);
-                return false;
-            }
-        }
-    }
-}
-
 // ---- TMA (cp.async.bulk.tensor) -------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap *map) {
@@ -343,24 +310,6 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// Named barrier that also ORs a predicate over the `count` threads: every
-// thread gets the same answer, so a decision to stop that any one thread
-// takes (or any thread sees in a flag that other roles may raise at any
-// moment) is taken by all of them together, and none is left waiting at a
-// later barrier for threads that have left.
-__device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t count, bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
-        : "memory");
-    return r != 0;
-}
-
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -390,15 +339,6 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 
 __device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
-}
-
-// 16 bytes into the shared memory of a CTA of this cluster (its address from
-// mapa_shared).
-__device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b,
-                                                     uint32_t c, uint32_t d) {
-    asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a), "r"(b),
-                 "r"(c), "r"(d)
-                 : "memory");
 }
 
 // All threads of all CTAs of the cluster.
