@@ -268,11 +268,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int slot = (x == r0) ? 0 : 1;  // a partial segment is the range's first or last
             x = seg_end;
             const int n = t * BN_T + nl;
-            // The four warps decide together whether to go on: a warp that
-            // gave up has raised the abort flag before this barrier.
+            // The four warps decide together whether to go on (a barrier that
+            // ORs every thread's answer: the abort flag may be raised by
+            // another role while they read it).
             const bool ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull);
-            named_bar_sync(1, 128);
-            if (!ok || *abort_flag) break;
+            if (named_bar_or(1, 128, !ok || *abort_flag != 0)) break;
             tc_fence_after_sync();
             // This thread's column of the accumulator, read from TMEM sixteen
             // rows at a time wherever it is needed; the accumulator is handed

@@ -310,6 +310,24 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ORs a predicate over the `count` threads: every
+// thread gets the same answer, so a decision to stop that any one thread
+// takes (or any thread sees in a flag that other roles may raise at any
+// moment) is taken by all of them together, and none is left waiting at a
+// later barrier for threads that have left.
+__device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
