@@ -32,6 +32,12 @@ namespace cudair {
 namespace {
 
 constexpr int kMaxBlocks = 64;
+// Tiles per side of C when B comes from the host (see the tiling rule in
+// cudair_gemm_f16f32_host).
+#ifndef CUDAIR_HOST_TILES
+#define CUDAIR_HOST_TILES 4
+#endif
+constexpr int kTilesPerSide = CUDAIR_HOST_TILES;
 
 struct HostPipe {
     cudaStream_t in = nullptr, out = nullptr;
@@ -120,8 +126,8 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
     int64_t rb = rows_per_block, cb = N;
     if (rb == 0) {
         if (b_host && K > 0 && N >= 4096 && M >= 1024) {
-            rb = (M + 3) / 4;
-            cb = ((N + 3) / 4 + 255) / 256 * 256;
+            rb = (M + kTilesPerSide - 1) / kTilesPerSide;
+            cb = ((N + kTilesPerSide - 1) / kTilesPerSide + 255) / 256 * 256;
         } else {
             rb = (M + 15) / 16;
         }
