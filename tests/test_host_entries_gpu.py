@@ -70,3 +70,41 @@ def test_matmul16_host(dev, oracle, n):
     assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
     from cudair import kernels as k
     assert k.wait_status(clear=True) == 0
+
+
+def test_host_entries_allocate_no_device_memory(dev):
+    # After a first call on the device (which creates the library's streams
+    # and events), further calls of the three host-buffer entries leave the
+    # device's free memory and torch's reserved bytes unchanged.
+    import torch
+    from cudair import kernels
+    n = 1 << 20
+    a_h, b_h, o_h = (torch.ones(n).pin_memory() for _ in range(3))
+    a_d, b_d, o_d = (torch.empty(n, device=dev) for _ in range(3))
+    m = 1024
+    ga_h = torch.ones(m, m, dtype=torch.float16).pin_memory()
+    gb_h = torch.ones(m, m, dtype=torch.float16).pin_memory()
+    gc_h = torch.zeros(m, m).pin_memory()
+    ga_d, gb_d = (torch.empty(m, m, dtype=torch.float16, device=dev) for _ in range(2))
+    gc_d = torch.empty(m, m, device=dev)
+    s = 256
+    sa_h = torch.ones(s, s, dtype=torch.float16).pin_memory()
+    sb_h = torch.ones(s, s, dtype=torch.float16).pin_memory()
+    sc_h = torch.zeros(s, s).pin_memory()
+    sa_d, sb_d = (torch.empty(s, s, dtype=torch.float16, device=dev) for _ in range(2))
+    sc_d = torch.empty(s, s, device=dev)
+
+    def calls():
+        kernels.vecadd_host(a_h, b_h, o_h, a_d, b_d, o_d)
+        kernels.gemm_host(ga_h, gb_h, gc_h, ga_d, gb_d, gc_d)
+        kernels.matmul16_host(sa_h, sb_h, sc_h, sa_d, sb_d, sc_d)
+        torch.cuda.synchronize()
+
+    calls()
+    free0, _ = torch.cuda.mem_get_info()
+    held0 = torch.cuda.memory_reserved()
+    calls()
+    calls()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert torch.cuda.memory_reserved() == held0
+    assert torch.equal(o_h, torch.full((n,), 2.0))

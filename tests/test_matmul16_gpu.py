@@ -214,11 +214,15 @@ def test_gemm_8192_cube_seeded(dev, cudair, oracle, variant):
     ref = (da.float() @ db.float()).add_(torch.from_numpy(c).to(dev)).cpu().numpy()
     rel, mx, bad = oracle.error_norms(got, ref)
     assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
-    # (2) sampled rows against the CPU oracle (fp32, every tile row-block hit).
-    rows = np.unique(np.concatenate([np.arange(0, n, 257), [n - 1]]))
-    for r in rows[::4]:
-        want = oracle.gemm_ikj(af, bf, c, rows=(int(r), int(r) + 1))
-        rel, mx, bad = oracle.error_norms(got[r:r + 1], want)
+    # (2) rows against the CPU oracle (fp32): every 257th row (each 256-row
+    # pair tile and 128-row CTA half hit at a different offset) and both
+    # sides of the tile boundaries at the start, middle and end.
+    edges = [0, 1, 127, 128, 255, 256, 511, 512, n // 2 - 1, n // 2, n - 257, n - 256, n - 129, n - 128,
+             n - 2, n - 1]
+    rows = np.unique(np.concatenate([np.arange(0, n, 257), edges]))
+    want = oracle.gemm_ikj(np.ascontiguousarray(af[rows]), bf, np.ascontiguousarray(c[rows]))
+    for i, r in enumerate(rows):
+        rel, mx, bad = oracle.error_norms(got[r:r + 1], want[i:i + 1])
         assert bad == 0 and rel <= tol_rel and mx <= tol_max, (r, rel, mx)
 
 
