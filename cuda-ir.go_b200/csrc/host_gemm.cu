@@ -38,6 +38,16 @@ constexpr int kMaxBlocks = 64;
 #define CUDAIR_HOST_TILES 4
 #endif
 constexpr int kTilesPerSide = CUDAIR_HOST_TILES;
+// With kHostEdge > 0, the first and last row and column blocks are that many
+// rows / columns, around kHostInner even blocks.
+#ifndef CUDAIR_HOST_EDGE
+#define CUDAIR_HOST_EDGE 0
+#endif
+#ifndef CUDAIR_HOST_INNER
+#define CUDAIR_HOST_INNER 2
+#endif
+constexpr int64_t kHostEdge = CUDAIR_HOST_EDGE;
+constexpr int kHostInner = CUDAIR_HOST_INNER;
 
 struct HostPipe {
     cudaStream_t in = nullptr, out = nullptr;
@@ -123,20 +133,42 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
     // last block (the part of the call nothing overlaps) stays short.  An
     // explicit rows_per_block asks for full-width row blocks of that height.
     // At most kMaxBlocks tiles.
-    int64_t rb = rows_per_block, cb = N;
-    if (rb == 0) {
-        if (b_host && K > 0 && N >= 4096 && M >= 1024) {
-            rb = (M + kTilesPerSide - 1) / kTilesPerSide;
-            cb = ((N + kTilesPerSide - 1) / kTilesPerSide + 255) / 256 * 256;
+    // Block boundaries along M (rows) and N (columns).
+    int64_t rbnd[kMaxBlocks + 1], cbnd[kMaxBlocks + 1];
+    auto even = [](int64_t L, int64_t blk, int64_t *b) -> int {
+        int nb = 0;
+        b[0] = 0;
+        for (int64_t x = 0; x < L; x += blk) b[++nb] = (x + blk < L) ? x + blk : L;
+        return nb;
+    };
+    // A short first and last block around `inner` even middle blocks (256
+    // multiples): the first tile's inputs and the last tile's output, the
+    // parts of the call that nothing else overlaps, stay small.
+    auto edged = [](int64_t L, int64_t edge, int inner, int64_t *b) -> int {
+        int nb = 0;
+        b[0] = 0;
+        b[++nb] = edge;
+        const int64_t blk = ((L - 2 * edge + inner - 1) / inner + 255) / 256 * 256;
+        for (int64_t x = edge; x < L - edge; x += blk) b[++nb] = (x + blk < L - edge) ? x + blk : L - edge;
+        b[++nb] = L;
+        return nb;
+    };
+    int row_blocks = 0, col_blocks = 0;
+    if (rows_per_block == 0 && b_host && K > 0 && N >= 4096 && M >= 1024) {
+        if (kHostEdge > 0 && M >= 4 * kHostEdge && N >= 4 * kHostEdge) {
+            row_blocks = edged(M, kHostEdge, kHostInner, rbnd);
+            col_blocks = edged(N, kHostEdge, kHostInner, cbnd);
         } else {
-            rb = (M + 15) / 16;
+            row_blocks = even(M, ((M + kTilesPerSide - 1) / kTilesPerSide + 255) / 256 * 256, rbnd);
+            col_blocks = even(N, ((N + kTilesPerSide - 1) / kTilesPerSide + 255) / 256 * 256, cbnd);
         }
+    } else {
+        int64_t rb = rows_per_block > 0 ? rows_per_block : (M + 15) / 16;
+        rb = (rb + 255) / 256 * 256;
+        if ((M + rb - 1) / rb > kMaxBlocks) rb = ((M + kMaxBlocks - 1) / kMaxBlocks + 255) / 256 * 256;
+        row_blocks = even(M, rb, rbnd);
+        col_blocks = even(N, N, cbnd);
     }
-    rb = (rb + 255) / 256 * 256;
-    const int col_blocks = static_cast<int>((N + cb - 1) / cb);
-    if ((M + rb - 1) / rb * col_blocks > kMaxBlocks)
-        rb = ((M + kMaxBlocks / col_blocks - 1) / (kMaxBlocks / col_blocks) + 255) / 256 * 256;
-    const int row_blocks = static_cast<int>((M + rb - 1) / rb);
 
     int sms = 0;
     int rc = sm_count_current_device(&sms);  // device and primary-context checks
@@ -160,7 +192,7 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
                  c_row = static_cast<size_t>(N) * 4;
     int t = 0;
     for (int j = 0; j < col_blocks; ++j) {
-        const int64_t n0 = j * cb, cols = (N - n0 < cb) ? N - n0 : cb;
+        const int64_t n0 = cbnd[j], cols = cbnd[j + 1] - cbnd[j];
         if (K > 0 && b_host)
             CUDAIR_TRY(copy_rows(static_cast<uint8_t *>(b_dev) + static_cast<size_t>(n0) * 2, b_row,
                                  static_cast<const uint8_t *>(b_host) + static_cast<size_t>(n0) * 2,
@@ -168,7 +200,7 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
                                  static_cast<size_t>(K), cudaMemcpyHostToDevice, p->in),
                        "H2D of B");
         for (int i = 0; i < row_blocks; ++i, ++t) {
-            const int64_t r0 = i * rb, rows = (M - r0 < rb) ? M - r0 : rb;
+            const int64_t r0 = rbnd[i], rows = rbnd[i + 1] - rbnd[i];
             uint8_t *a_blk = static_cast<uint8_t *>(a_dev) + static_cast<size_t>(r0) * a_row;
             float *c_tile = c_dev + static_cast<size_t>(r0) * N + n0;
             float *c_host_tile = c_host + static_cast<size_t>(r0) * ldc + n0;
