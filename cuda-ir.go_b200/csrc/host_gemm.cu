@@ -38,16 +38,6 @@ constexpr int kMaxBlocks = 64;
 #define CUDAIR_HOST_TILES 4
 #endif
 constexpr int kTilesPerSide = CUDAIR_HOST_TILES;
-// With kHostEdge > 0, the first and last row and column blocks are that many
-// rows / columns, around kHostInner even blocks.
-#ifndef CUDAIR_HOST_EDGE
-#define CUDAIR_HOST_EDGE 0
-#endif
-#ifndef CUDAIR_HOST_INNER
-#define CUDAIR_HOST_INNER 2
-#endif
-constexpr int64_t kHostEdge = CUDAIR_HOST_EDGE;
-constexpr int kHostInner = CUDAIR_HOST_INNER;
 
 struct HostPipe {
     cudaStream_t in = nullptr, out = nullptr;
@@ -141,27 +131,12 @@ CUDAIR_API int cudair_gemm_f16f32_host(const void *a_host, const void *b_host, f
         for (int64_t x = 0; x < L; x += blk) b[++nb] = (x + blk < L) ? x + blk : L;
         return nb;
     };
-    // A short first and last block around `inner` even middle blocks (256
-    // multiples): the first tile's inputs and the last tile's output, the
-    // parts of the call that nothing else overlaps, stay small.
-    auto edged = [](int64_t L, int64_t edge, int inner, int64_t *b) -> int {
-        int nb = 0;
-        b[0] = 0;
-        b[++nb] = edge;
-        const int64_t blk = ((L - 2 * edge + inner - 1) / inner + 255) / 256 * 256;
-        for (int64_t x = edge; x < L - edge; x += blk) b[++nb] = (x + blk < L - edge) ? x + blk : L - edge;
-        b[++nb] = L;
-        return nb;
-    };
     int row_blocks = 0, col_blocks = 0;
     if (rows_per_block == 0 && b_host && K > 0 && N >= 4096 && M >= 1024) {
-        if (kHostEdge > 0 && M >= 4 * kHostEdge && N >= 4 * kHostEdge) {
-            row_blocks = edged(M, kHostEdge, kHostInner, rbnd);
-            col_blocks = edged(N, kHostEdge, kHostInner, cbnd);
-        } else {
-            row_blocks = even(M, ((M + kTilesPerSide - 1) / kTilesPerSide + 255) / 256 * 256, rbnd);
-            col_blocks = even(N, ((N + kTilesPerSide - 1) / kTilesPerSide + 255) / 256 * 256, cbnd);
-        }
+        // Even 2D tiles.  Finer ones (6 x 6, 8 x 8) and a short first and
+        // last block were measured slower or equal at 8192^3.
+        row_blocks = even(M, ((M + kTilesPerSide - 1) / kTilesPerSide + 255) / 256 * 256, rbnd);
+        col_blocks = even(N, ((N + kTilesPerSide - 1) / kTilesPerSide + 255) / 256 * 256, cbnd);
     } else {
         int64_t rb = rows_per_block > 0 ? rows_per_block : (M + 15) / 16;
         rb = (rb + 255) / 256 * 256;
