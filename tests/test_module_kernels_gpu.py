@@ -7,8 +7,10 @@ launched the way the reference's tests do, with the same known answers:
   TestLaunchEx (hostapi_test.go:360-466): RuntimeClusterDims,
       ProgrammaticDependentLaunch, Cooperative
   examples/vecadd/run/main.go:62-76: Saxpy, Square
-  TestTensor (tensor_test.go:23-145): MmaF16, MmaF16Bias, MmaF16Trans,
-      MmaF16Half, MmaBF16
+  TestTensor (tensor_test.go:23-326): MmaF16, MmaF16Bias, MmaF16Trans,
+      MmaF16Half, MmaBF16, MmaTF32, MmaTF32Trans, MmaS8, MmaU8,
+      LdMatrixRegs, MmaLdMatrix, WmmaBF16, WmmaBF16Trans, WmmaTF32, WmmaS8,
+      WmmaU8
 """
 import ctypes
 
@@ -288,3 +290,188 @@ def test_mma_bf16(dev, mod, tensor_kat):
     launch(mod, "MmaBF16", _mma_cfg(n), host.ArgBuffer(ab), host.ArgBuffer(bb), host.ArgBuffer(dc),
            host.ArgValue(ctypes.c_int32(n)))
     assert np.array_equal(dc.cpu().numpy(), want)
+
+
+# ---- TestTensor: tf32, int8, ldmatrix and wmma (tensor_test.go:147-326) -------
+
+def _wmma_cfg(n):
+    return cfg1d((n // 16) * (n // 16) * 32, 128)
+
+
+def _int8_kat(n):
+    # tensor_test.go:161-169 and 293-305: signed operands are the float KAT's
+    # values, unsigned ones other elem() patterns, bt the transpose of bu
+    au = _elem(n, 7, 13, 3, 5).astype(np.uint8)
+    bu = _elem(n, 11, 5, 7, 3).astype(np.uint8)
+    bias_i = (_elem(n, 3, 7, 5, 11) - 5).astype(np.int32)
+    return au, bu, np.ascontiguousarray(bu.T), bias_i
+
+
+def test_mma_tf32(dev, mod, tensor_kat):
+    from cudair import host
+    n, af, bf, _, want = tensor_kat
+    da, db, dbt = up(dev, af), up(dev, bf), up(dev, np.ascontiguousarray(bf.T))
+    n32 = host.ArgValue(ctypes.c_int32(n))
+    dc = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "MmaTF32", _mma_cfg(n), host.ArgBuffer(da), host.ArgBuffer(db), host.ArgBuffer(dc), n32)
+    assert np.array_equal(dc.cpu().numpy(), want)
+    dc2 = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "MmaTF32Trans", _mma_cfg(n), host.ArgBuffer(da), host.ArgBuffer(dbt), host.ArgBuffer(dc2), n32)
+    assert np.array_equal(dc2.cpu().numpy(), want)
+
+
+def test_mma_tf32_rounds_inputs(dev, mod):
+    # cvt.rna keeps 10 mantissa bits, ties away from zero: 1 + 2^-11 (a tie)
+    # becomes 1 + 2^-10 and 1 + 2^-12 becomes 1, so one 16 x 8 tile of A = that
+    # value, B = identity shows the rounding the reference asks for.
+    from cudair import host
+    n = 16
+    a = np.zeros((n, n), np.float32)
+    a[:, 0] = 1 + 2.0 ** -11
+    a[:, 1] = 1 + 2.0 ** -12
+    a[:, 2] = -(1 + 2.0 ** -11)
+    b = np.eye(n, dtype=np.float32)
+    dc = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "MmaTF32", _mma_cfg(n), host.ArgBuffer(up(dev, a)), host.ArgBuffer(up(dev, b)),
+           host.ArgBuffer(dc), host.ArgValue(ctypes.c_int32(n)))
+    got = dc.cpu().numpy()
+    assert np.all(got[:, 0] == np.float32(1 + 2.0 ** -10))
+    assert np.all(got[:, 1] == np.float32(1.0))
+    assert np.all(got[:, 2] == np.float32(-(1 + 2.0 ** -10)))
+    assert np.all(got[:, 3:] == 0)
+
+
+def test_mma_int8(dev, mod, tensor_kat):
+    from cudair import host
+    n, af, bf, _, _ = tensor_kat
+    a_s, b_s = af.astype(np.int8), bf.astype(np.int8)
+    au, bu, but, _ = _int8_kat(n)
+    want_s = a_s.astype(np.int64) @ b_s.astype(np.int64)
+    want_u = au.astype(np.int64) @ bu.astype(np.int64)
+    n32 = host.ArgValue(ctypes.c_int32(n))
+    dc = up(dev, np.zeros((n, n), np.int32))
+    launch(mod, "MmaS8", _mma_cfg(n), host.ArgBuffer(up(dev, a_s)), host.ArgBuffer(up(dev, b_s)),
+           host.ArgBuffer(dc), n32)
+    assert np.array_equal(dc.cpu().numpy(), want_s)
+    dc2 = up(dev, np.zeros((n, n), np.int32))
+    launch(mod, "MmaU8", _mma_cfg(n), host.ArgBuffer(up(dev, au)), host.ArgBuffer(up(dev, but)),
+           host.ArgBuffer(dc2), n32)
+    assert np.array_equal(dc2.cpu().numpy(), want_u)
+
+
+def test_mma_int8_full_range(dev, mod):
+    # every byte value, n = 128 (four k steps of 32): the s8 product, and the
+    # u8 one whose sums stay far below the .satfinite limit
+    from cudair import host
+    n = 128
+    rng = np.random.default_rng(5)
+    a = rng.integers(0, 256, (n, n), dtype=np.uint8)
+    b = rng.integers(0, 256, (n, n), dtype=np.uint8)
+    n32 = host.ArgValue(ctypes.c_int32(n))
+    dc = up(dev, np.zeros((n, n), np.int32))
+    launch(mod, "MmaS8", _mma_cfg(n), host.ArgBuffer(up(dev, a.view(np.int8))),
+           host.ArgBuffer(up(dev, b.view(np.int8))), host.ArgBuffer(dc), n32)
+    assert np.array_equal(dc.cpu().numpy(), a.view(np.int8).astype(np.int64) @ b.view(np.int8).astype(np.int64))
+    dc2 = up(dev, np.zeros((n, n), np.int32))
+    launch(mod, "MmaU8", _mma_cfg(n), host.ArgBuffer(up(dev, a)), host.ArgBuffer(up(dev, np.ascontiguousarray(b.T))),
+           host.ArgBuffer(dc2), n32)
+    assert np.array_equal(dc2.cpu().numpy(), a.astype(np.int64) @ b.astype(np.int64))
+
+
+def test_ldmatrix_registers(dev, mod, oracle):
+    # tensor_test.go:192-228: four 8 x 8 matrices of distinct halves; lane
+    # g*4+s holds (g, 2s), (g, 2s+1) of matrix i in register i (x4), the
+    # transposed pair in .trans, matrices 0-1 in x2 and matrix 0 in x1
+    from cudair import host
+    vals = oracle.f32_to_f16(np.arange(1, 4 * 64 + 1, dtype=np.float32)).astype(np.uint32)
+    dout = up(dev, np.zeros(4 * 32 * 4, np.int32))
+    launch(mod, "LdMatrixRegs", cfg1d(32, 32), host.ArgBuffer(up(dev, vals.astype(np.uint16).view(np.int16))),
+           host.ArgBuffer(dout))
+    out = dout.cpu().numpy().view(np.uint32)
+    mats = vals.reshape(4, 8, 8)
+    lane = np.arange(32)
+    g, s = lane // 4, lane % 4
+    for i in range(4):
+        m = mats[i]
+        assert np.array_equal(out[lane * 4 + i], m[g, 2 * s] | (m[g, 2 * s + 1] << 16))
+        assert np.array_equal(out[128 + lane * 4 + i], m[2 * s, g] | (m[2 * s + 1, g] << 16))
+    for i in range(2):
+        m = mats[i]
+        assert np.array_equal(out[256 + lane * 2 + i], m[g, 2 * s] | (m[g, 2 * s + 1] << 16))
+    assert np.array_equal(out[384 + lane], mats[0][g, 2 * s] | (mats[0][g, 2 * s + 1] << 16))
+
+
+def test_mma_ldmatrix(dev, mod, oracle):
+    # tensor_test.go:230-261
+    from cudair import host
+    i16 = np.arange(16).reshape(16, 1)
+    j16, j8 = np.arange(16).reshape(1, 16), np.arange(8).reshape(1, 8)
+    a16 = ((5 * i16 + 11 * j16 + 3 * i16 * j16) % 7 - 3).astype(np.float32)
+    b16 = ((13 * i16 + 7 * j8 + 5 * i16 * j8) % 5 - 2).astype(np.float32)
+    want = (a16.astype(np.int64) @ b16.astype(np.int64)).astype(np.float32)
+    dc = up(dev, np.zeros((16, 8), np.float32))
+    launch(mod, "MmaLdMatrix", cfg1d(32, 32), host.ArgBuffer(up(dev, oracle.f32_to_f16(a16).view(np.int16))),
+           host.ArgBuffer(up(dev, oracle.f32_to_f16(b16).view(np.int16))), host.ArgBuffer(dc))
+    assert np.array_equal(dc.cpu().numpy(), want)
+
+
+def test_wmma_bf16(dev, mod, tensor_kat):
+    from cudair import host
+    n, af, bf, bias, want = tensor_kat
+    da = up(dev, _bf16_bits(af).view(np.int16))
+    db = up(dev, _bf16_bits(bf).view(np.int16))
+    dbt = up(dev, _bf16_bits(np.ascontiguousarray(bf.T)).view(np.int16))
+    n32 = host.ArgValue(ctypes.c_int32(n))
+    dc = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "WmmaBF16", _wmma_cfg(n), host.ArgBuffer(da), host.ArgBuffer(db), host.ArgBuffer(up(dev, bias)),
+           host.ArgBuffer(dc), n32)
+    assert np.array_equal(dc.cpu().numpy(), want + bias)
+    dc2 = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "WmmaBF16Trans", _wmma_cfg(n), host.ArgBuffer(da), host.ArgBuffer(dbt), host.ArgBuffer(dc2), n32)
+    assert np.array_equal(dc2.cpu().numpy(), want)
+
+
+def test_wmma_tf32(dev, mod, tensor_kat):
+    from cudair import host
+    n, af, bf, _, want = tensor_kat
+    dc = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "WmmaTF32", _wmma_cfg(n), host.ArgBuffer(up(dev, af)), host.ArgBuffer(up(dev, bf)),
+           host.ArgBuffer(dc), host.ArgValue(ctypes.c_int32(n)))
+    assert np.array_equal(dc.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("n", [64, 48])
+def test_wmma_int8(dev, mod, n):
+    # n = 48: an odd number of 16-byte k steps and odd column tiles, the
+    # cases whose tiles sit only 16 bytes apart in global memory
+    from cudair import host
+    af = (_elem(n, 7, 13, 3, 5) - 2).astype(np.int8)
+    bf = (_elem(n, 11, 5, 7, 5) - 2).astype(np.int8)
+    au, bu, but, bias_i = _int8_kat(n)
+    want_s = af.astype(np.int64) @ bf.astype(np.int64)
+    want_u = bias_i + au.astype(np.int64) @ bu.astype(np.int64)
+    n32 = host.ArgValue(ctypes.c_int32(n))
+    dc = up(dev, np.zeros((n, n), np.int32))
+    launch(mod, "WmmaS8", _wmma_cfg(n), host.ArgBuffer(up(dev, af)), host.ArgBuffer(up(dev, bf)),
+           host.ArgBuffer(dc), n32)
+    assert np.array_equal(dc.cpu().numpy(), want_s)
+    dc2 = up(dev, np.zeros((n, n), np.int32))
+    launch(mod, "WmmaU8", _wmma_cfg(n), host.ArgBuffer(up(dev, au)), host.ArgBuffer(up(dev, but)),
+           host.ArgBuffer(up(dev, bias_i)), host.ArgBuffer(dc2), n32)
+    assert np.array_equal(dc2.cpu().numpy(), want_u)
+
+
+def test_tensor_kernels_refuse_bad_shapes(dev, mod):
+    # n not a multiple of 16, or of the int8 mma's k step of 32: the kernels
+    # return without writing.  The buffers hold 64 x 64, so a kernel that
+    # went ahead would still stay inside them.
+    from cudair import host
+    import torch
+    a = up(dev, np.ones((64, 64), np.int8))
+    dc = up(dev, np.full((64, 64), 7, np.int32))
+    for name, cfg, n in (("MmaS8", _mma_cfg(64), 48), ("MmaU8", _mma_cfg(64), 40),
+                         ("WmmaS8", _wmma_cfg(64), 40)):
+        launch(mod, name, cfg, host.ArgBuffer(a), host.ArgBuffer(a), host.ArgBuffer(dc),
+               host.ArgValue(ctypes.c_int32(n)))
+    torch.cuda.synchronize()
+    assert np.all(dc.cpu().numpy() == 7)
