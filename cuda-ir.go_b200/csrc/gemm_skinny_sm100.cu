@@ -26,9 +26,16 @@
 // Roles as in gemm_sm100.cu (192 threads): warp 0 TMA producer, warp 1 TMEM
 // owner and MMA issuer, warps 2-5 epilogue and fix-up.  All waits are
 // bounded.
+//
+// A second kernel below (gemm_chunked_kernel, M <= 32) keeps the swap of
+// operands and the ring but replaces the static ranges by fixed k-chunks
+// that the CTAs take at run time; chunked_auto_chunks picks it for the
+// shapes where it measured faster.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "cudair_internal.h"
@@ -390,6 +397,385 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+
+// ---- dynamically scheduled variant: fixed k-chunks handed out by ticket ----
+//
+// The stream-K kernel above gives every CTA the same share of B.  In a chain
+// of launches the CTAs do not start together (a CTA takes an SM when the
+// preceding launch's CTA on it exits) and do not stream at the same rate, so
+// the last MMAs of one launch spread over several microseconds, and every
+// tile split between two late CTAs waits for both.  This variant cuts each
+// 128-column n-tile into S fixed k-chunks and hands the chunks out at run
+// time: CTA c takes chunk c first (so it may request that chunk's B before
+// the dependency wait), then the next ticket of a counter in the workspace,
+// one chunk ahead of its loads.  A CTA that started late or streams slowly
+// simply takes fewer chunks.  Chunks are numbered tile by tile, so a tile's
+// chunks run at about the same time and the tiles complete all through the
+// launch, not at its end.
+//
+// Every chunk's fp32 part is summed into C by the tile's last chunk to
+// finish, in chunk order: C + part_0 + ... + part_{S-1}.  The chunk bounds
+// depend only on the shape, so the result does not depend on which CTA ran
+// which chunk, nor on timing.  As in the stream-K fix-up, the last chunk
+// checks the tile's counter first and, when it is last, adds its own part
+// straight from TMEM.  The last CTA to finish resets the ticket for the next
+// launch, which reads it only after its dependency wait.
+constexpr int QDEPTH = 4;             // chunk ids in flight from the producer to the consumers
+constexpr int NACC = 4;               // TMEM accumulators: the MMA runs up to three chunks ahead
+constexpr uint32_t CH_BAR_BYTES = 512;
+constexpr int CH_MAX_MPAD = 32;
+
+__host__ __device__ constexpr int ch_stages_for(int mpad) {
+    return static_cast<int>((SMEM_BYTES - 1024 - CH_BAR_BYTES) / (B_STAGE_BYTES + mpad * BK * 2)) < MAX_STAGES
+               ? static_cast<int>((SMEM_BYTES - 1024 - CH_BAR_BYTES) / (B_STAGE_BYTES + mpad * BK * 2))
+               : MAX_STAGES;
+}
+__host__ __device__ constexpr size_t ch_smem_for(int mpad) {
+    return 1024 + static_cast<size_t>(ch_stages_for(mpad)) * (B_STAGE_BYTES + mpad * BK * 2) + CH_BAR_BYTES;
+}
+static_assert(ch_smem_for(16) <= SMEM_BYTES && ch_smem_for(CH_MAX_MPAD) <= SMEM_BYTES, "shared memory budget");
+static_assert(2 * MAX_STAGES * 8 + (2 * NACC + 1) * 8 + 2 * QDEPTH * 8 + 16 + QDEPTH * 4 <= CH_BAR_BYTES,
+              "barrier area");
+
+// k-blocks [kb0, kb1) of chunk s of S over num_kb k-blocks.
+__host__ __device__ __forceinline__ int chunk_kb(int s, int S, int num_kb) {
+    return static_cast<int>((static_cast<long long>(s) * num_kb) / S);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_chunked_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA,
+                        float *__restrict__ C, int M, int N, int K, long long ldc, int mpad, int S,
+                        unsigned int *__restrict__ counters, unsigned int *__restrict__ sched,
+                        float *__restrict__ partials, unsigned int *status, int b_early) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+    const uint32_t a_stage_bytes = static_cast<uint32_t>(mpad) * BK * 2;  // multiple of 1024
+    const int STAGES = ch_stages_for(mpad);
+    uint8_t *sB = smem;
+    uint8_t *sA = smem + STAGES * B_STAGE_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sA + STAGES * a_stage_bytes);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + STAGES;
+    uint64_t *acc_full = bars + 2 * STAGES;
+    uint64_t *acc_empty = acc_full + NACC;
+    uint64_t *drain = acc_empty + NACC;
+    uint64_t *q_full = drain + 1;
+    uint64_t *q_empty = q_full + QDEPTH;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(q_empty + QDEPTH);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    volatile int *last_flag = abort_flag + 1;
+    volatile int *q_ring = last_flag + 1;
+
+    const uint32_t warp = warp_id(), lane = lane_id();
+    const int n_tiles = (N + BN_T - 1) / BN_T;
+    const int num_kb = (K + BK - 1) / BK;
+    const int total = n_tiles * S;
+    const int G = static_cast<int>(gridDim.x);
+    const int c = static_cast<int>(blockIdx.x);
+    const uint32_t tmem_cols = mpad <= 16 ? 64u : 128u;  // NACC accumulators of mpad columns
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < NACC; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(drain, 1);
+        for (int i = 0; i < QDEPTH; ++i) {
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 5);  // the MMA thread and the four epilogue warps
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_map(&tmA);
+        tma_prefetch_map(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+    if (threadIdx.x == 0) grid_launch_dependents();
+
+    if (warp == 0) {
+        // ---------------- TMA producer and scheduler ----------------
+        if (lane == 0) {
+            const uint64_t policy_b = l2_policy_evict_normal();
+            const uint64_t policy_a = l2_policy_evict_last();  // A is re-read by every chunk
+            uint32_t stage = 0, phase = 0, issued = 0;
+            bool ok = true;
+            int q = c < total ? c : -1;
+            int kb_start = q >= 0 ? chunk_kb(q % S, S, num_kb) : 0;
+            if (b_early && q >= 0) {
+                // B does not depend on the preceding kernel (the caller's
+                // promise): the first ring of this CTA's first chunk is
+                // requested before the dependency wait, A after it.
+                const int t = q / S, kb1 = chunk_kb(q % S + 1, S, num_kb);
+                const int pre = min(kb1 - kb_start, STAGES);
+                const int n0 = t * BN_T, nb = (n0 + 64 < N) ? 2 : 1;
+                for (int i = 0; i < pre; ++i) {
+                    mbar_arrive_expect_tx(&full[i], nb * B_BOX_BYTES + a_stage_bytes);
+                    for (int j = 0; j < nb; ++j)
+                        tma_load_2d(sB + i * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB, &full[i], n0 + 64 * j,
+                                    (kb_start + i) * BK, policy_b);
+                }
+                grid_dependency_wait();
+                for (int i = 0; i < pre; ++i)
+                    tma_load_2d(sA + i * a_stage_bytes, &tmA, &full[i], (kb_start + i) * BK, 0, policy_a);
+                issued = static_cast<uint32_t>(pre);
+                stage = issued % static_cast<uint32_t>(STAGES);
+                phase = (issued == static_cast<uint32_t>(STAGES)) ? 1u : 0u;
+                kb_start += pre;
+            } else {
+                grid_dependency_wait();
+            }
+            for (int j = 0; ok; ++j) {
+                // Hand the chunk (or the end, -1) to the MMA thread and the
+                // epilogue.
+                const int slot = j % QDEPTH;
+                if (!mbar_wait(&q_empty[slot], ((j / QDEPTH) & 1) ^ 1, abort_flag, status, kSiteProducerEmpty)) {
+                    ok = false;
+                    break;
+                }
+                q_ring[slot] = q;
+                mbar_arrive(&q_full[slot]);
+                if (q < 0) break;
+                // The next chunk, taken one chunk ahead of its loads.
+                const int next = total > G ? G + static_cast<int>(atomicAdd(&sched[0], 1u)) : total;
+                const int t = q / S, kb1 = chunk_kb(q % S + 1, S, num_kb);
+                const int n0 = t * BN_T, nb = (n0 + 64 < N) ? 2 : 1;  // skip a box wholly beyond N
+                for (int kb = kb_start; kb < kb1; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, kSiteProducerEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], nb * B_BOX_BYTES + a_stage_bytes);
+                    for (int jj = 0; jj < nb; ++jj)
+                        tma_load_2d(sB + stage * B_STAGE_BYTES + jj * B_BOX_BYTES, &tmB, &full[stage],
+                                    n0 + 64 * jj, kb * BK, policy_b);
+                    tma_load_2d(sA + stage * a_stage_bytes, &tmA, &full[stage], kb * BK, 0, policy_a);
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                q = next < total ? next : -1;
+                kb_start = q >= 0 ? chunk_kb(q % S, S, num_kb) : 0;
+            }
+            if (!ok) {
+                const uint32_t outstanding = issued < STAGES ? issued : STAGES;
+                for (uint32_t i = 1; i <= outstanding; ++i) {
+                    const uint32_t idx = issued - i;
+                    int never = 0;
+                    mbar_wait(&full[idx % STAGES], (idx / STAGES) & 1u, &never, status, kSiteDrain);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            grid_dependency_wait();
+            const uint32_t idesc = idesc_f16_f32(BN_T, static_cast<uint32_t>(mpad), true, false);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true, issued_any = false;
+            for (int j = 0; ok; ++j) {
+                const int slot = j % QDEPTH;
+                if (!mbar_wait(&q_full[slot], (j / QDEPTH) & 1, abort_flag, status, kSiteMmaFull)) {
+                    ok = false;
+                    break;
+                }
+                const int q = q_ring[slot];
+                mbar_arrive(&q_empty[slot]);
+                if (q < 0) break;
+                const int kb0 = chunk_kb(q % S, S, num_kb), kb1 = chunk_kb(q % S + 1, S, num_kb);
+                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, status, kSiteMmaAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after_sync();
+                const uint32_t d_tmem = tmem_base + acc * static_cast<uint32_t>(mpad);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, status, kSiteMmaFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after_sync();
+                    const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
+                    const uint32_t a_base = smem_u32(sA + stage * a_stage_bytes);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t b_desc = smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
+                        const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                        umma_f16_ss(d_tmem, b_desc, a_desc, idesc, (kb == kb0 && kk == 0) ? 0u : 1u);
+                    }
+                    issued_any = true;
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[acc]);
+                if (++acc == NACC) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (!ok && issued_any) {
+                umma_commit(drain);
+                int never = 0;
+                mbar_wait(drain, 0, &never, status, kSiteDrain);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue and tile sums (warps 2..5) ----------------
+        // Each chunk's accumulator is read into registers and handed back to
+        // the MMA at once; the memory round trips that follow (the tile
+        // counter, the part's visibility, the sum) then delay only this
+        // role, not the tensor pipe.  The counter is read when the chunk id
+        // arrives, long before the accumulator does.
+        grid_dependency_wait();  // C and the workspace may be the preceding kernel's
+        const uint32_t qw = warp & 3u;
+        const int nl = static_cast<int>(qw * 32 + lane);  // n within the tile
+        const bool leader = (warp == 2 && lane == 0);
+        const int chunks16 = mpad / 16;  // 1 or 2
+        uint32_t acc = 0, acc_phase = 0;
+        for (int j = 0;; ++j) {
+            const int slot = j % QDEPTH;
+            const bool got = mbar_wait(&q_full[slot], (j / QDEPTH) & 1, abort_flag, status, kSiteEpilogueAccFull);
+            if (named_bar_or(1, 128, !got || *abort_flag != 0)) break;
+            const int q = q_ring[slot];
+            named_bar_sync(1, 128);  // every thread has read the slot
+            if (lane == 0) mbar_arrive(&q_empty[slot]);
+            if (q < 0) break;
+            const int t = q / S, s = q % S;
+            const int n = t * BN_T + nl;
+            const unsigned int others = static_cast<unsigned int>(S - 1);
+            unsigned int pre = 0;
+            if (leader && S > 1) pre = ld_relaxed_gpu_u32(&counters[t]);
+            const bool ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull);
+            if (named_bar_or(1, 128, !ok || *abort_flag != 0)) break;
+            tc_fence_after_sync();
+            const uint32_t t_row = tmem_base + ((qw * 32u) << 16) + acc * static_cast<uint32_t>(mpad);
+            uint32_t r[2][16];
+            tmem_ld_32x32b_x16(t_row, r[0]);
+            if (chunks16 > 1) tmem_ld_32x32b_x16(t_row + 16, r[1]);
+            tmem_ld_wait();
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            if (++acc == NACC) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+            if (S == 1) {
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    if (jj >= chunks16 || n >= N) break;
+                    float v[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        v[i] = (16 * jj + i < M) ? C[static_cast<long long>(16 * jj + i) * ldc + n] : 0.f;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        if (16 * jj + i < M)
+                            C[static_cast<long long>(16 * jj + i) * ldc + n] = v[i] + __uint_as_float(r[jj][i]);
+                }
+                continue;
+            }
+            if (leader) *last_flag = (pre == others) ? 1 : 0;
+            named_bar_sync(1, 128);
+            bool last = *last_flag != 0;
+            if (!last) {
+                float *part = partials + static_cast<size_t>(q) * BN_T * mpad;
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    if (jj >= chunks16) break;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) part[(16 * jj + i) * BN_T + nl] = __uint_as_float(r[jj][i]);
+                }
+                // The part is published by one release: the barrier orders
+                // every thread's stores before the leader's fence and count.
+                named_bar_sync(1, 128);
+                if (leader) {
+                    __threadfence();
+                    const unsigned int prev = atomicAdd(&counters[t], 1u);
+                    *last_flag = (prev == others) ? 1 : 0;
+                }
+                named_bar_sync(1, 128);
+                last = *last_flag != 0;
+            }
+            if (last) {
+                __threadfence();  // acquire: the other chunks' parts are visible from here
+                // Sixteen rows at a time: C, then the parts in chunk order,
+                // four loaded together (this chunk's own from registers).
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    if (jj >= chunks16 || 16 * jj >= M || n >= N) break;
+                    float v[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        v[i] = (16 * jj + i < M) ? C[static_cast<long long>(16 * jj + i) * ldc + n] : 0.f;
+                    for (int sb = 0; sb < S; sb += 4) {
+                        float pv[4][16];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const int ss = sb + k;
+                            if (ss >= S || ss == s) continue;
+                            const float *pc = partials + static_cast<size_t>(t * S + ss) * BN_T * mpad;
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                pv[k][i] = (16 * jj + i < M) ? __ldcg(pc + (16 * jj + i) * BN_T + nl) : 0.f;
+                        }
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const int ss = sb + k;
+                            if (ss >= S) break;
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) v[i] += (ss == s) ? __uint_as_float(r[jj][i]) : pv[k][i];
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        if (16 * jj + i < M) C[static_cast<long long>(16 * jj + i) * ldc + n] = v[i];
+                }
+                if (leader) counters[t] = 0u;
+            }
+            named_bar_sync(1, 128);  // last_flag is reused by the next chunk
+        }
+        __syncwarp();
+    }
+
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem_base, tmem_cols);
+    }
+    // The last CTA out resets the ticket for the next launch: every CTA has
+    // taken its last ticket before it counts itself out here.
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&sched[1], 1u) == static_cast<unsigned int>(G - 1)) {
+            sched[0] = 0u;
+            sched[1] = 0u;
+            __threadfence();
+        }
+    }
+}
+
 }  // namespace skinny
 
 namespace {
@@ -402,10 +788,12 @@ struct Workspace {
 std::mutex g_ws_mu;
 Workspace g_ws[64];
 
-// Tile counters, then two partial slots (128 x M fp32) per CTA for up to 160
-// CTAs at M = 128: 21.25 MB.
+// Tile counters, the chunked variant's ticket and exit counter (1 KiB), then
+// the partial sums: two slots (128 x M fp32) per CTA for up to 160 CTAs at
+// M = 128, or one slot per chunk of the chunked variant: 21.25 MB.
+constexpr size_t kSchedBytes = 1024;
 constexpr size_t kWorkspaceBytes =
-    skinny::COUNTER_BYTES + 160u * 2u * skinny::BN_T * skinny::MAX_M * sizeof(float);
+    skinny::COUNTER_BYTES + kSchedBytes + 160u * 2u * skinny::BN_T * skinny::MAX_M * sizeof(float);
 
 // The library's per-device workspace of the skinny kernel (tile counters +
 // partial slots), allocated and zeroed on the first call on a device.
@@ -432,6 +820,9 @@ int workspace(Workspace **out) {
         e = cudaFuncSetAttribute(skinny::gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(skinny::SMEM_BYTES));
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(skinny)");
+        e = cudaFuncSetAttribute(skinny::gemm_chunked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(skinny::SMEM_BYTES));
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(chunked)");
         w.attr_set = true;
     }
     *out = &w;
@@ -512,16 +903,141 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
     }
     const long long T = static_cast<long long>(n_tiles) * ((K + skinny::BK - 1) / skinny::BK);
     // One CTA per SM, as many as there are units and as the partial slots hold.
-    const long long slots_fit = static_cast<long long>(ws->bytes - skinny::COUNTER_BYTES) /
+    const long long slots_fit = static_cast<long long>(ws->bytes - skinny::COUNTER_BYTES - kSchedBytes) /
                                 (2LL * skinny::BN_T * mpad * static_cast<long long>(sizeof(float)));
     long long g = T < sm_count ? T : sm_count;
     if (g > slots_fit) g = slots_fit;
     const int grid = static_cast<int>(g);
     unsigned int *counters = static_cast<unsigned int *>(ws->ptr);
-    float *partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws->ptr) + skinny::COUNTER_BYTES);
+    float *partials =
+        reinterpret_cast<float *>(static_cast<uint8_t *>(ws->ptr) + skinny::COUNTER_BYTES + kSchedBytes);
     cudaError_t e = launch_skinny(grid, skinny::smem_for(mpad), stream, gemm_pdl_mode(), tmB, tmA, c, M, N,
                                   K, static_cast<long long>(ldc), mpad, counters, partials, status);
     if (e != cudaSuccess) return cuda_error(e, "gemm_skinny_kernel launch");
+    return CUDAIR_OK;
+}
+
+// The automatic choice between the two few-row kernels, from measurements on
+// a B200 (148 SMs) of M = 1, 16 and 32 with N from 1024 to 57344 and K from
+// 4096 to 28672, each kernel in a chain of 30 launches with B requested
+// early.  Returns the chunks per n-tile for the chunked kernel, or 0 for the
+// stream-K kernel.
+//   * At most half as many 128-column tiles as SMs: G / n_tiles chunks per
+//     tile, so every CTA runs one chunk and every tile has the same number of
+//     equal parts.  5-16 % faster than stream-K at 8 to 64 tiles (stream-K
+//     gives each tile four to eighteen uneven contributors, several of them
+//     finishing together at the end).
+//   * More tiles: chunks are handed out in waves of G, and a last wave that
+//     is less than half full leaves the HBM to a few SMs at the end.  Two
+//     chunks per tile are used when the last wave is 50-97 % full or there
+//     are at least four waves (e.g. 112 tiles: 1.51 waves, 1.5 % faster; 448
+//     tiles: 6.05 waves, 4-6 %); three (M <= 16 only; at M = 32 three chunks
+//     were slower everywhere) when that gives a last wave 50-97 % full (96
+//     tiles: 1.95 waves, 8 %).  Otherwise stream-K (e.g. 148 or 160 tiles,
+//     2.0 and 2.16 waves at two chunks).
+//   * Chunks are at least four k-blocks long.
+int chunked_auto_chunks(int M, int N, int K, int sm_count) {
+    const int mpad = (M + 15) / 16 * 16;
+    if (mpad > skinny::CH_MAX_MPAD || sm_count < 2) return 0;
+    const long long n_tiles = (N + skinny::BN_T - 1) / skinny::BN_T;
+    const long long max_s = ((K + skinny::BK - 1) / skinny::BK) / 4;
+    if (2 * n_tiles <= sm_count) {
+        const long long S = std::min(static_cast<long long>(sm_count) / n_tiles, max_s);
+        return S >= 2 ? static_cast<int>(S) : 0;
+    }
+    auto last_wave_ok = [&](long long S) {
+        const long long total = n_tiles * S;
+        const long long part = total % sm_count;  // chunks in the last wave
+        return 2 * part >= sm_count && 100 * part <= 97LL * sm_count;
+    };
+    if (max_s >= 2 && (last_wave_ok(2) || 2 * n_tiles >= 4LL * sm_count)) return 2;
+    if (mpad <= 16 && max_s >= 3 && last_wave_ok(3)) return 3;
+    return 0;
+}
+
+// Chunks per n-tile for a launch of the chunked kernel: `chunks` when > 0,
+// else the automatic count (two where the automatic rule would run
+// stream-K); CUDAIR_FEWROWS_CHUNKS, when set, overrides both.  At most one
+// chunk per k-block and no more chunks than the partial slots hold.
+int chunked_chunks(int chunks, int M, int N, int K, int grid, size_t partial_bytes) {
+    const int mpad = (M + 15) / 16 * 16;
+    const int n_tiles = (N + skinny::BN_T - 1) / skinny::BN_T;
+    const int num_kb = (K + skinny::BK - 1) / skinny::BK;
+    long long S = chunks > 0 ? chunks : chunked_auto_chunks(M, N, K, grid);
+    if (S <= 0) S = 2;
+    if (const char *env = std::getenv("CUDAIR_FEWROWS_CHUNKS")) {
+        const long long v = std::atoll(env);
+        if (v > 0) S = v;
+    }
+    if (S > num_kb) S = num_kb;
+    const long long fit =
+        static_cast<long long>(partial_bytes / (static_cast<size_t>(skinny::BN_T) * mpad * sizeof(float))) / n_tiles;
+    if (S > fit) S = fit;
+    return S < 1 ? 1 : static_cast<int>(S);
+}
+
+int gemm_chunked_launch(const void *a, const void *b, float *c, int M, int N, int K, int64_t lda,
+                        int64_t ldb, int64_t ldc, int chunks, int sm_count, unsigned int *status,
+                        cudaStream_t stream) {
+    if (M < 1 || M > skinny::CH_MAX_MPAD)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm: the chunked few-row kernel takes 1 <= M <= %d, got %d",
+                         skinny::CH_MAX_MPAD, M);
+    const int n_tiles = (N + skinny::BN_T - 1) / skinny::BN_T;
+    if (n_tiles > skinny::MAX_TILES)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: N = %d too large for the few-row kernel", N);
+    Workspace *ws = nullptr;
+    int rc = workspace(&ws);
+    if (rc != CUDAIR_OK) return rc;
+    const int mpad = (M + 15) / 16 * 16;
+    const size_t partial_bytes = ws->bytes - skinny::COUNTER_BYTES - kSchedBytes;
+    if (static_cast<size_t>(n_tiles) * skinny::BN_T * mpad * sizeof(float) > partial_bytes)
+        return set_error(CUDAIR_ERR_INVALID, "cudair: gemm: N = %d too large for the chunked kernel", N);
+
+    alignas(64) CUtensorMap tmB, tmA;
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(K)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+        const uint32_t box[2] = {64, skinny::BK};
+        rc = encode_tiled_internal(&tmB, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(b),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+        const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+        const uint32_t box[2] = {skinny::BK, static_cast<uint32_t>(mpad)};
+        rc = encode_tiled_internal(&tmA, CUDAIR_TENSOR_MAP_FLOAT16, 2, reinterpret_cast<uint64_t>(a),
+                                   dims, strides, box, nullptr, CUDAIR_INTERLEAVE_NONE,
+                                   CUDAIR_SWIZZLE_128B, CUDAIR_L2_PROMOTION_256B, CUDAIR_OOB_FILL_NONE);
+        if (rc != CUDAIR_OK) return rc;
+    }
+    const int S = chunked_chunks(chunks, M, N, K, sm_count, partial_bytes);
+    const long long total = static_cast<long long>(n_tiles) * S;
+    const int grid = static_cast<int>(total < sm_count ? total : sm_count);
+    uint8_t *base = static_cast<uint8_t *>(ws->ptr);
+    unsigned int *counters = reinterpret_cast<unsigned int *>(base);
+    unsigned int *sched = reinterpret_cast<unsigned int *>(base + skinny::COUNTER_BYTES);
+    float *partials = reinterpret_cast<float *>(base + skinny::COUNTER_BYTES + kSchedBytes);
+
+    const int pdl = gemm_pdl_mode();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(skinny::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = skinny::ch_smem_for(mpad);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (pdl > 0) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, skinny::gemm_chunked_kernel, tmB, tmA, c, M, N, K,
+                                       static_cast<long long>(ldc), mpad, S, counters, sched, partials, status,
+                                       pdl == 2 ? 1 : 0);
+    if (e != cudaSuccess) return cuda_error(e, "gemm_chunked_kernel launch");
     return CUDAIR_OK;
 }
 

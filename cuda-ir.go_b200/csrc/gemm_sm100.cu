@@ -752,7 +752,7 @@ struct DeviceInfo {
 
 std::mutex g_dev_mu;
 DeviceInfo g_dev[64];
-std::atomic<int> g_variant{0};  // 0 auto, 1 single CTA, 2 CTA pair
+std::atomic<int> g_variant{0};  // 0 auto, 1 single CTA, 2 CTA pair, ... (cudair_set_gemm_variant)
 std::atomic<int> g_pdl{0};      // 0 plain launch, 1 PDL, 2 PDL with B early (few-row kernel)
 
 int device_info(DeviceInfo **out) {
@@ -1006,9 +1006,13 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
     // tile) cost more than the single-CTA kernel's idle SMs (measured: at
     // M = 128, K = 8192: 51.0 against 54.6 us for N = 8192; at K = 4096,
     // 47.5 against 33.2 us for N = 14336).
-    if (variant == 3 && flags != 0)
+    if ((variant == 3 || variant == 6) && flags != 0)
         return set_error(CUDAIR_ERR_INVALID,
-                         "cudair: gemm: the few-row kernel (variant 3) takes only the plain form (flags 0)");
+                         "cudair: gemm: the few-row kernels (variants 3 and 6) take only the plain form (flags 0)");
+    if (variant == 6 && M > 32)
+        return set_error(CUDAIR_ERR_INVALID,
+                         "cudair: gemm: the chunked few-row kernel (variant 6) takes M <= 32, got %lld",
+                         (long long)M);
     if (variant == 5 && (flags != 0 || K > 64 * kSmallMaxKBlocks))
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm: the small-problem kernel (variant 5) takes the plain form (flags 0) "
@@ -1029,6 +1033,15 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
     const bool fewrows_auto = variant == 0 && flags == 0 && !small_auto && (M <= 64 || (M <= 128 && N <= 8192)) &&
                               units >= dev->sm_count;
     const int use_variant = small_auto ? 5 : variant;
+    // The few-row kernels: with fixed k-chunks handed out at run time where
+    // that measured faster (chunked_auto_chunks), else stream-K.
+    const int chunks = fewrows_auto ? chunked_auto_chunks(static_cast<int>(M), static_cast<int>(N),
+                                                          static_cast<int>(K), dev->sm_count)
+                                    : 0;
+    if (variant == 6 || chunks > 0)
+        return gemm_chunked_launch(a, b, static_cast<float *>(c), static_cast<int>(M), static_cast<int>(N),
+                                   static_cast<int>(K), lda, ldb, ldc, chunks, dev->sm_count, dev->status,
+                                   stream);
     if (variant == 3 || fewrows_auto)
         return gemm_skinny_launch(a, b, static_cast<float *>(c), static_cast<int>(M), static_cast<int>(N),
                                   static_cast<int>(K), lda, ldb, ldc, dev->sm_count, dev->status,
@@ -1151,10 +1164,11 @@ CUDAIR_API int cudair_gemm(const void *a, const void *b, void *c, const float *b
 
 CUDAIR_API int cudair_set_gemm_variant(int variant) {
     clear_error();
-    if (variant < 0 || variant > 5)
+    if (variant < 0 || variant > 6)
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm variant %d, want 0 (auto), 1 (single CTA), 2 (CTA pair), "
-                         "3 (few rows), 4 (CTA pair, 256 x 512 tiles) or 5 (small problems, K <= 512)",
+                         "3 (few rows), 4 (CTA pair, 256 x 512 tiles), 5 (small problems, K <= 512) "
+                         "or 6 (few rows, chunks handed out at run time, M <= 32)",
                          variant);
     g_variant.store(variant);
     return CUDAIR_OK;

@@ -1,7 +1,8 @@
-// module_demos.cuh - the remaining entry points of the reference's hopper and
-// vecadd example packages, with the reference's names and parameter ABI, so
-// the module is a drop-in for those packages' tests (TestHopper,
-// TestTensorMap, TestLaunchEx, the vecadd run program).
+// module_demos.cuh - the remaining entry points of the reference's hopper,
+// vecadd and tensor example packages and the wmma GEMMs of its advanced
+// package, with the reference's names and parameter ABI, so the module is a
+// drop-in for those packages' tests (TestHopper, TestTensorMap, TestLaunchEx,
+// TestTensor, the Wmma case of TestAdvanced, the vecadd run program).
 //
 // Every wait on an mbarrier here is bounded (kDemoWaitNs); a wait that runs
 // out gives up and the kernel returns, leaving its outputs unwritten, which
@@ -708,7 +709,8 @@ extern "C" __global__ void MmaLdMatrix(const uint16_t *a, const uint16_t *b, flo
     store_acc(c, 8, acc);
 }
 
-// ---- tensor package: wmma with bf16, tf32, s8 and u8 (examples/tensor/tensor.go:238-330) ----
+// ---- wmma: tensor package (bf16, tf32, s8, u8; examples/tensor/tensor.go:238-330) and the
+// advanced package's fp16 Wmma / WmmaTrans ----
 //
 // The reference's contract is one warp per 16 x 16 tile of C
 // (LaunchConfig1D((n/16)*(n/16)*32, 128)).  wmma fragment loads want 32-byte
@@ -789,6 +791,45 @@ extern "C" __global__ void WmmaBF16Trans(const __nv_bfloat16 *a, const __nv_bflo
         w::mma_sync(acc, fa, fb, acc);
     }
     w::store_matrix_sync(c + static_cast<int64_t>(tl.row) * 16 * n + tl.col * 16, acc, n, w::mem_row_major);
+}
+
+// C = A.B + Bias with fp16 inputs, the MatMul16 element types on wmma
+// (examples/advanced/advanced.go:11-27).
+extern "C" __global__ void Wmma(const __half *a, const __half *b, const float *bias, float *c, int n) {
+    using namespace cudair_tensor;
+    namespace w = nvcuda::wmma;
+    const Tile16 tl = tile16_of_warp(n);
+    if (!tl.ok || !aligned32(a, b, c, bias)) return;
+    const int64_t rc = static_cast<int64_t>(tl.row) * 16 * n + tl.col * 16;
+    w::fragment<w::accumulator, 16, 16, 16, float> acc;
+    w::load_matrix_sync(acc, bias + rc, n, w::mem_row_major);
+    for (int k = 0; k < n; k += 16) {
+        w::fragment<w::matrix_a, 16, 16, 16, __half, w::row_major> fa;
+        w::fragment<w::matrix_b, 16, 16, 16, __half, w::row_major> fb;
+        w::load_matrix_sync(fa, a + static_cast<int64_t>(tl.row) * 16 * n + k, n);
+        w::load_matrix_sync(fb, b + static_cast<int64_t>(k) * n + tl.col * 16, n);
+        w::mma_sync(acc, fa, fb, acc);
+    }
+    w::store_matrix_sync(c + rc, acc, n, w::mem_row_major);
+}
+
+// C = A.Bt^T with bt row-major (B read column-major), zero accumulator, and
+// C stored column-major: c[j*n + i] = C[i][j] (examples/advanced/advanced.go:29-46).
+extern "C" __global__ void WmmaTrans(const __half *a, const __half *bt, float *c, int n) {
+    using namespace cudair_tensor;
+    namespace w = nvcuda::wmma;
+    const Tile16 tl = tile16_of_warp(n);
+    if (!tl.ok || !aligned32(a, bt, c)) return;
+    w::fragment<w::accumulator, 16, 16, 16, float> acc;
+    w::fill_fragment(acc, 0.f);
+    for (int k = 0; k < n; k += 16) {
+        w::fragment<w::matrix_a, 16, 16, 16, __half, w::row_major> fa;
+        w::fragment<w::matrix_b, 16, 16, 16, __half, w::col_major> fb;
+        w::load_matrix_sync(fa, a + static_cast<int64_t>(tl.row) * 16 * n + k, n);
+        w::load_matrix_sync(fb, bt + static_cast<int64_t>(tl.col) * 16 * n + k, n);
+        w::mma_sync(acc, fa, fb, acc);
+    }
+    w::store_matrix_sync(c + static_cast<int64_t>(tl.col) * 16 * n + tl.row * 16, acc, n, w::mem_col_major);
 }
 
 // C = A.B, float32 inputs rounded to tf32, m16n16k8 so k steps of 8

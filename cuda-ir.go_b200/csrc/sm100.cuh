@@ -173,6 +173,15 @@ __device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int *p
     return v;
 }
 
+// Relaxed load at GPU scope: it orders nothing, so the thread does not wait
+// for it until it uses the value.  A caller that then reads what another CTA
+// published follows it with a fence (acquire) before those reads.
+__device__ __forceinline__ unsigned int ld_relaxed_gpu_u32(const unsigned int *p) {
+    unsigned int v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Programmatic dependent launch.  griddepcontrol.wait returns once the grids
 // this one depends on have completed and their memory is visible (at once
 // when the launch had no such dependency); launch_dependents lets the next

@@ -172,7 +172,8 @@ def matmul16_host(a_h, b_h, c_h, a_d, b_d, c_d, stream=None) -> None:
 def set_gemm_variant(variant: int) -> None:
     """0 = automatic, 1 = single-CTA 128x256 tiles, 2 = CTA-pair 256x256 tiles,
     3 = few-row kernel (M <= 128), 4 = CTA-pair 256x512 tiles, 5 = small-problem
-    kernel (K <= 512)."""
+    kernel (K <= 512), 6 = few-row kernel with k-chunks handed out at run time
+    (M <= 32)."""
     check(lib().cudair_set_gemm_variant(variant))
 
 

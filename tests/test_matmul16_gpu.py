@@ -33,12 +33,13 @@ def no_wait_timeouts(dev, cudair):
     assert kernels.wait_status(clear=True) == 0
 
 
-@pytest.fixture(params=[1, 2, 3, 4, 5], ids=["single", "pair", "fewrows", "pairwide", "small"])
+@pytest.fixture(params=[1, 2, 3, 4, 5, 6], ids=["single", "pair", "fewrows", "pairwide", "small", "chunked"])
 def variant(request, dev, cudair):
     """Runs a test on each GEMM kernel in turn: single CTA (128x256 tiles),
     CTA pair (256x256), the few-row kernel (M <= 128), the wide CTA pair
-    (256x512) and the small-problem kernel (K <= 512, one 128x64 tile per
-    CTA), then restores the automatic choice."""
+    (256x512), the small-problem kernel (K <= 512, one 128x64 tile per CTA)
+    and the chunked few-row kernel (M <= 32), then restores the automatic
+    choice."""
     from cudair import kernels
     kernels.set_gemm_variant(request.param)
     yield request.param
@@ -50,6 +51,8 @@ def _applies(variant, M, K=0):
         pytest.skip("the few-row kernel takes M <= 128")
     if variant == 5 and K > 512:
         pytest.skip("the small-problem kernel takes K <= 512")
+    if variant == 6 and M > 32:
+        pytest.skip("the chunked few-row kernel takes M <= 32")
 
 
 def kat(M, N, K):
@@ -296,7 +299,7 @@ def test_gemm_c_layouts(dev, cudair, variant, c_offset, ldc_pad):
     # Elements of C outside the view keep their value.
     import torch
     from cudair import kernels
-    M = 40 if variant == 3 else 300
+    M = 40 if variant == 3 else (24 if variant == 6 else 300)
     N, K = 101, 136
     af, bf, c, want = kat(M, N, K)
     A = _dev(af, dev, torch.float16)

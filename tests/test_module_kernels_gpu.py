@@ -11,6 +11,7 @@ launched the way the reference's tests do, with the same known answers:
       MmaF16Half, MmaBF16, MmaTF32, MmaTF32Trans, MmaS8, MmaU8,
       LdMatrixRegs, MmaLdMatrix, WmmaBF16, WmmaBF16Trans, WmmaTF32, WmmaS8,
       WmmaU8
+  TestAdvanced/Wmma (advanced_test.go:25-80): Wmma, WmmaTrans
 """
 import ctypes
 
@@ -475,3 +476,28 @@ def test_tensor_kernels_refuse_bad_shapes(dev, mod):
                host.ArgValue(ctypes.c_int32(n)))
     torch.cuda.synchronize()
     assert np.all(dc.cpu().numpy() == 7)
+
+
+# ---- TestAdvanced/Wmma (advanced_test.go:25-80) ----------------------------------
+
+def test_wmma_f16(dev, mod, oracle):
+    from cudair import host
+    n = 64
+    i = np.arange(n).reshape(n, 1)
+    j = np.arange(n).reshape(1, n)
+    af = ((i + j) % 5 - 2).astype(np.float32)
+    bf = ((i * j) % 3).astype(np.float32)
+    bias = (i - j).astype(np.float32)
+    prod = (af.astype(np.int64) @ bf.astype(np.int64)).astype(np.float32)
+    da = up(dev, oracle.f32_to_f16(af).view(np.int16))
+    db = up(dev, oracle.f32_to_f16(bf).view(np.int16))
+    dbt = up(dev, oracle.f32_to_f16(np.ascontiguousarray(bf.T)).view(np.int16))
+    n32 = host.ArgValue(ctypes.c_int32(n))
+    dc = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "Wmma", _wmma_cfg(n), host.ArgBuffer(da), host.ArgBuffer(db), host.ArgBuffer(up(dev, bias)),
+           host.ArgBuffer(dc), n32)
+    assert np.array_equal(dc.cpu().numpy(), prod + bias)
+    # WmmaTrans: B given transposed, no bias, C stored column-major
+    dc2 = up(dev, np.zeros((n, n), np.float32))
+    launch(mod, "WmmaTrans", _wmma_cfg(n), host.ArgBuffer(da), host.ArgBuffer(dbt), host.ArgBuffer(dc2), n32)
+    assert np.array_equal(dc2.cpu().numpy().T, prod)
