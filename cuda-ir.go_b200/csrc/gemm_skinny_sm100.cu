@@ -409,9 +409,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 // time: CTA c takes chunk c first (so it may request that chunk's B before
 // the dependency wait), then the next ticket of a counter in the workspace,
 // one chunk ahead of its loads.  A CTA that started late or streams slowly
-// simply takes fewer chunks.  Chunks are numbered tile by tile, so a tile's
-// chunks run at about the same time and the tiles complete all through the
-// launch, not at its end.
+// simply takes fewer chunks.  Chunks are numbered k-chunk by k-chunk (every
+// tile's first chunk, then every tile's second, ...), so the chunks taken
+// last belong to tiles whose other parts were done a wave earlier: the last
+// chunk of such a tile finds them published and sums the tile at once from
+// its registers, instead of publishing its own part and counting in.
 //
 // Every chunk's fp32 part is summed into C by the tile's last chunk to
 // finish, in chunk order: C + part_0 + ... + part_{S-1}.  The chunk bounds
@@ -513,12 +515,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t stage = 0, phase = 0, issued = 0;
             bool ok = true;
             int q = c < total ? c : -1;
-            int kb_start = q >= 0 ? chunk_kb(q % S, S, num_kb) : 0;
+            int kb_start = q >= 0 ? chunk_kb(q / n_tiles, S, num_kb) : 0;
             if (b_early && q >= 0) {
                 // B does not depend on the preceding kernel (the caller's
                 // promise): the first ring of this CTA's first chunk is
                 // requested before the dependency wait, A after it.
-                const int t = q / S, kb1 = chunk_kb(q % S + 1, S, num_kb);
+                const int t = q % n_tiles, kb1 = chunk_kb(q / n_tiles + 1, S, num_kb);
                 const int pre = min(kb1 - kb_start, STAGES);
                 const int n0 = t * BN_T, nb = (n0 + 64 < N) ? 2 : 1;
                 for (int i = 0; i < pre; ++i) {
@@ -550,7 +552,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (q < 0) break;
                 // The next chunk, taken one chunk ahead of its loads.
                 const int next = total > G ? G + static_cast<int>(atomicAdd(&sched[0], 1u)) : total;
-                const int t = q / S, kb1 = chunk_kb(q % S + 1, S, num_kb);
+                const int t = q % n_tiles, kb1 = chunk_kb(q / n_tiles + 1, S, num_kb);
                 const int n0 = t * BN_T, nb = (n0 + 64 < N) ? 2 : 1;  // skip a box wholly beyond N
                 for (int kb = kb_start; kb < kb1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status, kSiteProducerEmpty)) {
@@ -569,7 +571,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
                 q = next < total ? next : -1;
-                kb_start = q >= 0 ? chunk_kb(q % S, S, num_kb) : 0;
+                kb_start = q >= 0 ? chunk_kb(q / n_tiles, S, num_kb) : 0;
             }
             if (!ok) {
                 const uint32_t outstanding = issued < STAGES ? issued : STAGES;
@@ -597,7 +599,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int q = q_ring[slot];
                 mbar_arrive(&q_empty[slot]);
                 if (q < 0) break;
-                const int kb0 = chunk_kb(q % S, S, num_kb), kb1 = chunk_kb(q % S + 1, S, num_kb);
+                const int kb0 = chunk_kb(q / n_tiles, S, num_kb), kb1 = chunk_kb(q / n_tiles + 1, S, num_kb);
                 if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, status, kSiteMmaAccEmpty)) {
                     ok = false;
                     break;
@@ -660,7 +662,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             named_bar_sync(1, 128);  // every thread has read the slot
             if (lane == 0) mbar_arrive(&q_empty[slot]);
             if (q < 0) break;
-            const int t = q / S, s = q % S;
+            const int t = q % n_tiles, s = q / n_tiles;
             const int n = t * BN_T + nl;
             const unsigned int others = static_cast<unsigned int>(S - 1);
             unsigned int pre = 0;
@@ -695,7 +697,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 continue;
             }
-            if (leader) *last_flag = (pre == others) ? 1 : 0;
+            // The early read may predate the other chunks' counts: read again
+            // now (one load, against a publish, fence and count otherwise).
+            if (leader) {
+                if (pre != others) pre = ld_relaxed_gpu_u32(&counters[t]);
+                *last_flag = (pre == others) ? 1 : 0;
+            }
             named_bar_sync(1, 128);
             bool last = *last_flag != 0;
             if (!last) {
@@ -734,7 +741,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         for (int k = 0; k < 4; ++k) {
                             const int ss = sb + k;
                             if (ss >= S || ss == s) continue;
-                            const float *pc = partials + static_cast<size_t>(t * S + ss) * BN_T * mpad;
+                            const float *pc = partials + (static_cast<size_t>(ss) * n_tiles + t) * BN_T * mpad;
 #pragma unroll
                             for (int i = 0; i < 16; ++i)
                                 pv[k][i] = (16 * jj + i < M) ? __ldcg(pc + (16 * jj + i) * BN_T + nl) : 0.f;
@@ -919,40 +926,40 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
 
 // The automatic choice between the two few-row kernels, from measurements on
 // a B200 (148 SMs) of M = 1, 16 and 32 with N from 1024 to 57344 and K from
-// 4096 to 28672, each kernel in a chain of 30 launches with B requested
+// 4096 to 28672, each kernel in a chain of 20-30 launches with B requested
 // early.  Returns the chunks per n-tile for the chunked kernel, or 0 for the
-// stream-K kernel.
+// stream-K kernel (M > 32, or K under four k-blocks per chunk).
 //   * At most half as many 128-column tiles as SMs: G / n_tiles chunks per
-//     tile, so every CTA runs one chunk and every tile has the same number of
-//     equal parts.  5-16 % faster than stream-K at 8 to 64 tiles (stream-K
-//     gives each tile four to eighteen uneven contributors, several of them
-//     finishing together at the end).
-//   * More tiles: chunks are handed out in waves of G, and a last wave that
-//     is less than half full leaves the HBM to a few SMs at the end.  Two
-//     chunks per tile are used when the last wave is 50-97 % full or there
-//     are at least four waves (e.g. 112 tiles: 1.51 waves, 1.5 % faster; 448
-//     tiles: 6.05 waves, 4-6 %); three (M <= 16 only; at M = 32 three chunks
-//     were slower everywhere) when that gives a last wave 50-97 % full (96
-//     tiles: 1.95 waves, 8 %).  Otherwise stream-K (e.g. 148 or 160 tiles,
-//     2.0 and 2.16 waves at two chunks).
-//   * Chunks are at least four k-blocks long.
+//     tile, so every CTA runs one chunk and every tile has equal parts (8-16 %
+//     faster than stream-K at 8 to 64 tiles).
+//   * More tiles: the chunks run in waves of G, and a wave that is only
+//     partly full leaves the HBM to fewer SMs.  The count S in 2..4 (2..3 at
+//     M > 16) whose waves are fullest, n_tiles * S / (ceil(n_tiles * S / G) * G),
+//     wins, a smaller S when two are within 0.02 of each other.  That picked
+//     the measured best, or one within 2 %, at every tile count from 80 to
+//     448; against stream-K it is 3-12 % faster, except at M = 32 with 160
+//     or 256 tiles (1-4 % slower).
 int chunked_auto_chunks(int M, int N, int K, int sm_count) {
     const int mpad = (M + 15) / 16 * 16;
     if (mpad > skinny::CH_MAX_MPAD || sm_count < 2) return 0;
+    const long long G = sm_count;
     const long long n_tiles = (N + skinny::BN_T - 1) / skinny::BN_T;
-    const long long max_s = ((K + skinny::BK - 1) / skinny::BK) / 4;
-    if (2 * n_tiles <= sm_count) {
-        const long long S = std::min(static_cast<long long>(sm_count) / n_tiles, max_s);
+    const long long max_s = ((K + skinny::BK - 1) / skinny::BK) / 4;  // chunks of at least four k-blocks
+    if (2 * n_tiles <= G) {
+        const long long S = std::min(G / n_tiles, max_s);
         return S >= 2 ? static_cast<int>(S) : 0;
     }
-    auto last_wave_ok = [&](long long S) {
+    int best = 0;
+    double best_fill = 0.0;
+    for (long long S = 2; S <= (mpad <= 16 ? 4 : 3) && S <= max_s; ++S) {
         const long long total = n_tiles * S;
-        const long long part = total % sm_count;  // chunks in the last wave
-        return 2 * part >= sm_count && 100 * part <= 97LL * sm_count;
-    };
-    if (max_s >= 2 && (last_wave_ok(2) || 2 * n_tiles >= 4LL * sm_count)) return 2;
-    if (mpad <= 16 && max_s >= 3 && last_wave_ok(3)) return 3;
-    return 0;
+        const double fill = static_cast<double>(total) / static_cast<double>(((total + G - 1) / G) * G);
+        if (fill > best_fill + 0.02) {
+            best_fill = fill;
+            best = static_cast<int>(S);
+        }
+    }
+    return best;
 }
 
 // Chunks per n-tile for a launch of the chunked kernel: `chunks` when > 0,
