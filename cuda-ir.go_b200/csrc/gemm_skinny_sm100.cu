@@ -420,8 +420,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 // depend only on the shape, so the result does not depend on which CTA ran
 // which chunk, nor on timing.  As in the stream-K fix-up, the last chunk
 // checks the tile's counter first and, when it is last, adds its own part
-// straight from TMEM.  The last CTA to finish resets the ticket for the next
-// launch, which reads it only after its dependency wait.
+// straight from its registers.  Every CTA takes exactly one ticket past the
+// end, so the CTA that takes the last ticket value resets the counter for the
+// next launch, which reads it only after its dependency wait.
 constexpr int QDEPTH = 4;             // chunk ids in flight from the producer to the consumers
 constexpr int NACC = 4;               // TMEM accumulators: the MMA runs up to three chunks ahead
 constexpr uint32_t CH_BAR_BYTES = 512;
@@ -436,7 +437,7 @@ __host__ __device__ constexpr size_t ch_smem_for(int mpad) {
     return 1024 + static_cast<size_t>(ch_stages_for(mpad)) * (B_STAGE_BYTES + mpad * BK * 2) + CH_BAR_BYTES;
 }
 static_assert(ch_smem_for(16) <= SMEM_BYTES && ch_smem_for(CH_MAX_MPAD) <= SMEM_BYTES, "shared memory budget");
-static_assert(2 * MAX_STAGES * 8 + (2 * NACC + 1) * 8 + 2 * QDEPTH * 8 + 16 + QDEPTH * 4 <= CH_BAR_BYTES,
+static_assert(2 * MAX_STAGES * 8 + (2 * NACC + 1) * 8 + 2 * QDEPTH * 8 + 16 + QDEPTH * 4 + 4 <= CH_BAR_BYTES,
               "barrier area");
 
 // k-blocks [kb0, kb1) of chunk s of S over num_kb k-blocks.
@@ -469,6 +470,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     volatile int *last_flag = abort_flag + 1;
     volatile int *q_ring = last_flag + 1;
+    volatile int *pf_flag = q_ring + QDEPTH;
 
     const uint32_t warp = warp_id(), lane = lane_id();
     const int n_tiles = (N + BN_T - 1) / BN_T;
@@ -551,7 +553,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mbar_arrive(&q_full[slot]);
                 if (q < 0) break;
                 // The next chunk, taken one chunk ahead of its loads.
-                const int next = total > G ? G + static_cast<int>(atomicAdd(&sched[0], 1u)) : total;
+                const bool grab = total > G;
+                const unsigned int raw = grab ? atomicAdd(&sched[0], 1u) : 0u;
+                const int next = grab ? G + static_cast<int>(raw) : total;
                 const int t = q % n_tiles, kb1 = chunk_kb(q / n_tiles + 1, S, num_kb);
                 const int n0 = t * BN_T, nb = (n0 + 64 < N) ? 2 : 1;  // skip a box wholly beyond N
                 for (int kb = kb_start; kb < kb1; ++kb) {
@@ -572,6 +576,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 q = next < total ? next : -1;
                 kb_start = q >= 0 ? chunk_kb(q / n_tiles, S, num_kb) : 0;
+                // Every CTA takes exactly one ticket past the end, so the one
+                // that takes the last value (total - 1) takes the launch's last
+                // ticket: it resets the counter for the next launch, which reads
+                // it only after its dependency wait.
+                if (grab && raw == static_cast<unsigned int>(total - 1)) sched[0] = 0u;
             }
             if (!ok) {
                 const uint32_t outstanding = issued < STAGES ? issued : STAGES;
@@ -659,6 +668,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const bool got = mbar_wait(&q_full[slot], (j / QDEPTH) & 1, abort_flag, status, kSiteEpilogueAccFull);
             if (named_bar_or(1, 128, !got || *abort_flag != 0)) break;
             const int q = q_ring[slot];
+            if (leader) *pf_flag = 0;
             named_bar_sync(1, 128);  // every thread has read the slot
             if (lane == 0) mbar_arrive(&q_empty[slot]);
             if (q < 0) break;
@@ -667,7 +677,58 @@ __global__ void __launch_bounds__(THREADS, 1)
             const unsigned int others = static_cast<unsigned int>(S - 1);
             unsigned int pre = 0;
             if (leader && S > 1) pre = ld_relaxed_gpu_u32(&counters[t]);
-            const bool ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, status, kSiteEpilogueAccFull);
+            // Two chunks per tile at M <= 16: while the accumulator is being
+            // computed the leader watches the tile counter, and once the other
+            // chunk has published its part every thread loads C and that part,
+            // so the tile's sum after the last MMA waits on no memory.
+            const bool watch = (S == 2 && chunks16 == 1);
+            const float *other_part = partials + (static_cast<size_t>(1 - s) * n_tiles + t) * BN_T * mpad;
+            bool known = false;  // leader: the other part is published
+            bool have = false;   // this thread holds C and the other part
+            float cv[16], pv[16];
+            bool ok = true;
+            {
+                const uint32_t bar_a = smem_u32(&acc_full[acc]);
+                const uint64_t t0 = globaltimer_ns();
+                uint64_t next_poll = 0;
+                for (uint32_t it = 1;; ++it) {
+                    if (mbar_try_wait(bar_a, acc_phase)) break;
+                    if (watch) {
+                        if (leader && !known) {
+                            const uint64_t now = globaltimer_ns();
+                            if (now >= next_poll) {
+                                if (pre == others || ld_relaxed_gpu_u32(&counters[t]) == others) {
+                                    __threadfence();  // acquire
+                                    known = true;
+                                    *pf_flag = 1;
+                                }
+                                next_poll = now + 500;
+                            }
+                        }
+                        if (!have && *pf_flag != 0) {
+                            __threadfence();
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                cv[i] = (i < M && n < N) ? C[static_cast<long long>(i) * ldc + n] : 0.f;
+                                pv[i] = (i < M) ? __ldcg(other_part + i * BN_T + nl) : 0.f;
+                            }
+                            have = true;
+                        }
+                    }
+                    if ((it & 15u) == 0u) {
+                        if (*abort_flag) {
+                            ok = false;
+                            break;
+                        }
+                        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                            *abort_flag = 1;
+                            atomicOr(status, kSiteEpilogueAccFull);
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
+            }
             if (named_bar_or(1, 128, !ok || *abort_flag != 0)) break;
             tc_fence_after_sync();
             const uint32_t t_row = tmem_base + ((qw * 32u) << 16) + acc * static_cast<uint32_t>(mpad);
@@ -700,8 +761,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             // The early read may predate the other chunks' counts: read again
             // now (one load, against a publish, fence and count otherwise).
             if (leader) {
-                if (pre != others) pre = ld_relaxed_gpu_u32(&counters[t]);
-                *last_flag = (pre == others) ? 1 : 0;
+                if (!known && pre != others) pre = ld_relaxed_gpu_u32(&counters[t]);
+                *last_flag = (known || pre == others) ? 1 : 0;
             }
             named_bar_sync(1, 128);
             bool last = *last_flag != 0;
@@ -724,7 +785,28 @@ __global__ void __launch_bounds__(THREADS, 1)
                 named_bar_sync(1, 128);
                 last = *last_flag != 0;
             }
-            if (last) {
+            if (last && watch) {
+                if (!have) {
+                    __threadfence();  // acquire: the other part is visible from here
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        cv[i] = (i < M && n < N) ? C[static_cast<long long>(i) * ldc + n] : 0.f;
+                        pv[i] = (i < M) ? __ldcg(other_part + i * BN_T + nl) : 0.f;
+                    }
+                }
+                // C + part 0 + part 1, the order of the general sum below.
+                if (n < N) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float own = __uint_as_float(r[0][i]);
+                        float v = cv[i];
+                        v += (s == 0) ? own : pv[i];
+                        v += (s == 0) ? pv[i] : own;
+                        if (i < M) C[static_cast<long long>(i) * ldc + n] = v;
+                    }
+                }
+                if (leader) counters[t] = 0u;
+            } else if (last) {
                 __threadfence();  // acquire: the other chunks' parts are visible from here
                 // Sixteen rows at a time: C, then the parts in chunk order,
                 // four loaded together (this chunk's own from registers).
@@ -771,16 +853,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after_sync();
         tmem_dealloc(tmem_base, tmem_cols);
     }
-    // The last CTA out resets the ticket for the next launch: every CTA has
-    // taken its last ticket before it counts itself out here.
-    if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd(&sched[1], 1u) == static_cast<unsigned int>(G - 1)) {
-            sched[0] = 0u;
-            sched[1] = 0u;
-            __threadfence();
-        }
-    }
 }
 
 }  // namespace skinny
@@ -795,7 +867,7 @@ struct Workspace {
 std::mutex g_ws_mu;
 Workspace g_ws[64];
 
-// Tile counters, the chunked variant's ticket and exit counter (1 KiB), then
+// Tile counters, the chunked variant's ticket counter (in a 1 KiB block), then
 // the partial sums: two slots (128 x M fp32) per CTA for up to 160 CTAs at
 // M = 128, or one slot per chunk of the chunked variant: 21.25 MB.
 constexpr size_t kSchedBytes = 1024;
