@@ -118,3 +118,36 @@ def test_chunked_refuses_other_forms(dev, cudair):
         kernels.gemm(a, b, c)
     with pytest.raises(Exception, match="plain form"):
         kernels.gemm_ex(a[:16], b, c[:16], overwrite=True)
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 128, 4096), (1, 128, 8192), (32, 296, 2048), (7, 256, 1000)])
+def test_automatic_choice_narrow_long_k(dev, cudair, oracle, M, N, K):
+    # Fewer (128-column x 64-k) units than SMs at M <= 32: the automatic
+    # choice cuts K into chunks on the chunked kernel instead of streaming all
+    # of K through one SM.  Exact on the integer generator; on seeded data the
+    # same bits as the chunked kernel chosen explicitly (so that kernel ran)
+    # and within the oracle's tolerance.
+    import torch
+    from cudair import kernels
+    af, bf, c, want = kat(M, N, K)
+    kernels.set_gemm_variant(0)
+    dc = _dev(c, dev, torch.float32)
+    kernels.gemm(_dev(af, dev, torch.float16), _dev(bf, dev, torch.float16), dc)
+    assert np.array_equal(dc.cpu().numpy(), want)
+
+    a16, a32 = _seeded_normal_f16(oracle, M * K, 21, 1.0)
+    b16, b32 = _seeded_normal_f16(oracle, K * N, 22, 0.05)
+    c = oracle.uniform(M * N, 23).reshape(M, N)
+    da = torch.from_numpy(a16.view(np.int16)).to(dev).view(torch.float16).reshape(M, K)
+    db = torch.from_numpy(b16.view(np.int16)).to(dev).view(torch.float16).reshape(K, N)
+    outs = []
+    for variant in (0, 6):
+        kernels.set_gemm_variant(variant)
+        dc = torch.from_numpy(c.copy()).to(dev)
+        kernels.gemm(da, db, dc)
+        outs.append(dc.cpu().numpy())
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    want = oracle.gemm_ikj(a32.reshape(M, K), b32.reshape(K, N), c)
+    tol_rel, tol_max = oracle.gemm_tolerance(K, np.abs(a32).max(), np.abs(b32).max())
+    rel, mx, bad = oracle.error_norms(outs[0], want)
+    assert bad == 0 and rel <= tol_rel and mx <= tol_max, (rel, mx)
