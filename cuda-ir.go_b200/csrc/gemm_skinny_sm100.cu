@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 constexpr int QDEPTH = 4;             // chunk ids in flight from the producer to the consumers
 constexpr int NACC = 4;               // TMEM accumulators: the MMA runs up to three chunks ahead
 constexpr uint32_t CH_BAR_BYTES = 512;
-constexpr int CH_MAX_MPAD = 32;
+constexpr int CH_MAX_MPAD = 64;
 
 __host__ __device__ constexpr int ch_stages_for(int mpad) {
     return static_cast<int>((SMEM_BYTES - 1024 - CH_BAR_BYTES) / (B_STAGE_BYTES + mpad * BK * 2)) < MAX_STAGES
@@ -478,7 +478,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int total = n_tiles * S;
     const int G = static_cast<int>(gridDim.x);
     const int c = static_cast<int>(blockIdx.x);
-    const uint32_t tmem_cols = mpad <= 16 ? 64u : 128u;  // NACC accumulators of mpad columns
+    const uint32_t tmem_cols = mpad <= 16 ? 64u : mpad <= 32 ? 128u : 256u;  // NACC accumulators of mpad columns
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -661,7 +661,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t qw = warp & 3u;
         const int nl = static_cast<int>(qw * 32 + lane);  // n within the tile
         const bool leader = (warp == 2 && lane == 0);
-        const int chunks16 = mpad / 16;  // 1 or 2
+        const int chunks16 = mpad / 16;  // 1 to 4
         uint32_t acc = 0, acc_phase = 0;
         for (int j = 0;; ++j) {
             const int slot = j % QDEPTH;
@@ -732,30 +732,58 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (named_bar_or(1, 128, !ok || *abort_flag != 0)) break;
             tc_fence_after_sync();
             const uint32_t t_row = tmem_base + ((qw * 32u) << 16) + acc * static_cast<uint32_t>(mpad);
+            // Up to 32 rows the accumulator is read into registers and handed
+            // back to the MMA at once.  At 48 and 64 rows it stays in TMEM, is
+            // read one 16-row group at a time where it is needed, and is
+            // handed back once the chunk's part is published or its tile
+            // summed (with four accumulators the MMA still runs up to three
+            // chunks ahead).  Every TMEM read below is warp-uniform.
+            const bool hold = chunks16 > 2;
+            const uint32_t acc_used = acc;
+            auto hand_back = [&]() {
+                tc_fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc_used]);
+            };
             uint32_t r[2][16];
-            tmem_ld_32x32b_x16(t_row, r[0]);
-            if (chunks16 > 1) tmem_ld_32x32b_x16(t_row + 16, r[1]);
-            tmem_ld_wait();
-            tc_fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            if (!hold) {
+                tmem_ld_32x32b_x16(t_row, r[0]);
+                if (chunks16 > 1) tmem_ld_32x32b_x16(t_row + 16, r[1]);
+                tmem_ld_wait();
+                hand_back();
+            }
             if (++acc == NACC) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
+            // This thread's 16 accumulator values of row group jj.
+            auto own_group = [&](int jj, uint32_t (&g)[16]) {
+                if (hold) {
+                    tmem_ld_32x32b_x16(t_row + 16u * static_cast<uint32_t>(jj), g);
+                    tmem_ld_wait();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) g[i] = (jj == 0) ? r[0][i] : r[1][i];
+                }
+            };
             if (S == 1) {
 #pragma unroll
-                for (int jj = 0; jj < 2; ++jj) {
-                    if (jj >= chunks16 || n >= N) break;
-                    float v[16];
+                for (int jj = 0; jj < CH_MAX_MPAD / 16; ++jj) {
+                    if (jj >= chunks16 || 16 * jj >= M) break;
+                    uint32_t g[16];
+                    own_group(jj, g);
+                    if (n < N) {
+                        float v[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        v[i] = (16 * jj + i < M) ? C[static_cast<long long>(16 * jj + i) * ldc + n] : 0.f;
+                        for (int i = 0; i < 16; ++i)
+                            v[i] = (16 * jj + i < M) ? C[static_cast<long long>(16 * jj + i) * ldc + n] : 0.f;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        if (16 * jj + i < M)
-                            C[static_cast<long long>(16 * jj + i) * ldc + n] = v[i] + __uint_as_float(r[jj][i]);
+                        for (int i = 0; i < 16; ++i)
+                            if (16 * jj + i < M)
+                                C[static_cast<long long>(16 * jj + i) * ldc + n] = v[i] + __uint_as_float(g[i]);
+                    }
                 }
+                if (hold) hand_back();
                 continue;
             }
             // The early read may predate the other chunks' counts: read again
@@ -769,10 +797,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!last) {
                 float *part = partials + static_cast<size_t>(q) * BN_T * mpad;
 #pragma unroll
-                for (int jj = 0; jj < 2; ++jj) {
+                for (int jj = 0; jj < CH_MAX_MPAD / 16; ++jj) {
                     if (jj >= chunks16) break;
+                    uint32_t g[16];
+                    own_group(jj, g);
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) part[(16 * jj + i) * BN_T + nl] = __uint_as_float(r[jj][i]);
+                    for (int i = 0; i < 16; ++i) part[(16 * jj + i) * BN_T + nl] = __uint_as_float(g[i]);
                 }
                 // The part is published by one release: the barrier orders
                 // every thread's stores before the leader's fence and count.
@@ -811,8 +841,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // Sixteen rows at a time: C, then the parts in chunk order,
                 // four loaded together (this chunk's own from registers).
 #pragma unroll
-                for (int jj = 0; jj < 2; ++jj) {
-                    if (jj >= chunks16 || 16 * jj >= M || n >= N) break;
+                for (int jj = 0; jj < CH_MAX_MPAD / 16; ++jj) {
+                    if (jj >= chunks16 || 16 * jj >= M) break;
+                    uint32_t g[16];
+                    own_group(jj, g);
+                    if (n >= N) continue;
                     float v[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i)
@@ -833,7 +866,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             const int ss = sb + k;
                             if (ss >= S) break;
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) v[i] += (ss == s) ? __uint_as_float(r[jj][i]) : pv[k][i];
+                            for (int i = 0; i < 16; ++i) v[i] += (ss == s) ? __uint_as_float(g[i]) : pv[k][i];
                         }
                     }
 #pragma unroll
@@ -842,6 +875,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 if (leader) counters[t] = 0u;
             }
+            if (hold) hand_back();
             named_bar_sync(1, 128);  // last_flag is reused by the next chunk
         }
         __syncwarp();
@@ -1011,9 +1045,12 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
 //     the measured best, or one within 2 %, at every tile count from 80 to
 //     448; against stream-K it is 3-12 % faster, except at M = 32 with 160
 //     or 256 tiles (1-4 % slower).
+// The automatic choice takes the chunked kernel up to this many rows; the
+// kernel itself runs up to skinny::CH_MAX_MPAD (variant 6).
+constexpr int kChunkedAutoMaxM = 32;
 int chunked_auto_chunks(int M, int N, int K, int sm_count) {
     const int mpad = (M + 15) / 16 * 16;
-    if (mpad > skinny::CH_MAX_MPAD || sm_count < 2) return 0;
+    if (mpad > kChunkedAutoMaxM || sm_count < 2) return 0;
     const long long G = sm_count;
     const long long n_tiles = (N + skinny::BN_T - 1) / skinny::BN_T;
     const long long max_s = ((K + skinny::BK - 1) / skinny::BK) / 4;  // chunks of at least four k-blocks

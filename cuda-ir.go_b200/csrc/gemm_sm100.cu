@@ -1009,9 +1009,9 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
     if ((variant == 3 || variant == 6) && flags != 0)
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm: the few-row kernels (variants 3 and 6) take only the plain form (flags 0)");
-    if (variant == 6 && M > 32)
+    if (variant == 6 && M > 64)
         return set_error(CUDAIR_ERR_INVALID,
-                         "cudair: gemm: the chunked few-row kernel (variant 6) takes M <= 32, got %lld",
+                         "cudair: gemm: the chunked few-row kernel (variant 6) takes M <= 64, got %lld",
                          (long long)M);
     if (variant == 5 && (flags != 0 || K > 64 * kSmallMaxKBlocks))
         return set_error(CUDAIR_ERR_INVALID,
@@ -1176,7 +1176,7 @@ CUDAIR_API int cudair_set_gemm_variant(int variant) {
         return set_error(CUDAIR_ERR_INVALID,
                          "cudair: gemm variant %d, want 0 (auto), 1 (single CTA), 2 (CTA pair), "
                          "3 (few rows), 4 (CTA pair, 256 x 512 tiles), 5 (small problems, K <= 512) "
-                         "or 6 (few rows, chunks handed out at run time, M <= 32)",
+                         "or 6 (few rows, chunks handed out at run time, M <= 64)",
                          variant);
     g_variant.store(variant);
     return CUDAIR_OK;

@@ -173,7 +173,7 @@ def set_gemm_variant(variant: int) -> None:
     """0 = automatic, 1 = single-CTA 128x256 tiles, 2 = CTA-pair 256x256 tiles,
     3 = few-row kernel (M <= 128), 4 = CTA-pair 256x512 tiles, 5 = small-problem
     kernel (K <= 512), 6 = few-row kernel with k-chunks handed out at run time
-    (M <= 32)."""
+    (M <= 64)."""
     check(lib().cudair_set_gemm_variant(variant))
 
 

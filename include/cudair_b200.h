@@ -195,7 +195,9 @@ int cudair_gemm(const void *a, const void *b, void *c, const float *bias,
  * 0 = automatic (few-row kernel when M <= 64, and when M <= 128 with
  * N <= 8192, given one 128-column x 64-k unit of work per SM, in its
  * chunked form (6) for M <= 32 where the tile count fills the SMs with
- * whole waves of chunks, its stream-K form (3) otherwise; the
+ * whole waves of chunks, its stream-K form (3) otherwise; the chunked form
+ * also for M <= 32 with fewer such units than SMs when K splits into at
+ * least two chunks of four 64-k blocks (narrow N, long K); the
  * small-problem kernel when K <= 512 and its 128 x 64 tiles fit one wave;
  * single CTAs with 128 x 256 tiles for the rest of M <= 128; else CTA pairs
  * with 256 x 256 or 256 x 512 tiles, whichever a makespan estimate for the
@@ -203,7 +205,7 @@ int cudair_gemm(const void *a, const void *b, void *c, const float *bias,
  * 3 = few-row kernel (M <= 128 only), 4 = CTA pair with 256 x 512 tiles,
  * 5 = small-problem kernel (K <= 512; one 128 x 64 tile of C per CTA, the
  * whole K panel loaded at once), 6 = few-row kernel with fixed k-chunks
- * handed out to the SMs at run time (M <= 32).  All variants compute the
+ * handed out to the SMs at run time (M <= 64).  All variants compute the
  * same result within fp32 rounding; the choice only affects speed.
  *
  * The few-row kernel (B as the MMA's 128-row side, K split evenly over all

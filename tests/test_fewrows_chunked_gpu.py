@@ -1,4 +1,4 @@
-"""The chunked few-row GEMM (variant 6) on the B200: C = A.B + C for M <= 32
+"""The chunked few-row GEMM (variant 6) on the B200: C = A.B + C for M <= 64
 with each 128-column tile cut into fixed k-chunks that the SMs take at run
 time from a ticket counter, and each tile summed by its last chunk in chunk
 order.
@@ -67,16 +67,49 @@ def test_chunked_exact(dev, cudair, M, N, K, chunks):
         assert np.all(got[:, N:] == -9.0)
 
 
+@functools.lru_cache(maxsize=None)
+def _kat64(N, K):
+    return kat(64, N, K)
+
+
+@pytest.mark.parametrize("chunks", [None, 3, 64])
+@pytest.mark.parametrize("M", [33, 48, 64])
+@pytest.mark.parametrize("N,K", [(14336, 4096), (1001, 520), (300, 4104), (128, 64)])
+def test_chunked_exact_wide(dev, cudair, M, N, K, chunks):
+    # 33 to 64 rows: the accumulator stays in TMEM and is read 16 rows at a
+    # time where it is needed.  Exact, twice from the same C, padding untouched.
+    import torch
+    from cudair import kernels
+    if chunks is not None:
+        os.environ["CUDAIR_FEWROWS_CHUNKS"] = str(chunks)
+    af, bf, c, want = _kat64(N, K)
+    af, c, want = af[:M], c[:M], want[:M]
+    da = _dev(af, dev, torch.float16)
+    B = torch.zeros(K, (N + 7) // 8 * 8, dtype=torch.float16, device=dev)
+    B[:, :N] = _dev(bf, dev, torch.float16)
+    ldc = N + 4
+    for _ in range(2):
+        C = torch.full((M, ldc), -9.0, dtype=torch.float32, device=dev)
+        C[:, :N] = _dev(c, dev, torch.float32)
+        kernels.gemm(da, B[:, :N], C[:, :N])
+        got = C.cpu().numpy()
+        bad = np.argwhere(got[:, :N] != want)
+        assert bad.size == 0, (len(bad), tuple(bad[0]))
+        assert np.all(got[:, N:] == -9.0)
+
+
+@pytest.mark.parametrize("M", [16, 64])
 @pytest.mark.parametrize("pdl", [0, 1, 2])
-def test_chunked_chain_of_launches(dev, cudair, pdl):
+def test_chunked_chain_of_launches(dev, cudair, pdl, M):
     # Twenty launches back to back on one stream, with programmatic dependent
     # launch off, on, and on with B requested early: each launch must find the
     # ticket reset by the one before.  Integer data: C + 20 A.B exactly.
     import torch
     from cudair import kernels
     kernels.set_gemm_pdl(pdl)
-    M, N, K = 16, 14336, 4096
-    af, bf, c, want = kat(M, N, K)
+    N, K = 14336, 4096
+    af, bf, c, want = _kat64(N, K)
+    af, c, want = af[:M], c[:M], want[:M]
     da, db = _dev(af, dev, torch.float16), _dev(bf, dev, torch.float16)
     dc = _dev(c, dev, torch.float32)
     for _ in range(20):
@@ -85,12 +118,13 @@ def test_chunked_chain_of_launches(dev, cudair, pdl):
     assert np.array_equal(dc.cpu().numpy(), (c.astype(np.int64) + 20 * prod).astype(np.float32))
 
 
-def test_chunked_decode_shape_seeded(dev, cudair, oracle):
-    # M=16, N=14336, K=4096: A ~ N(0,1), B ~ N(0,0.02), C ~ U(-1,1), against
-    # the oracle within tolerance, and the same bits on a second run.
+@pytest.mark.parametrize("M", [16, 64])
+def test_chunked_decode_shape_seeded(dev, cudair, oracle, M):
+    # M x 14336 x 4096: A ~ N(0,1), B ~ N(0,0.02), C ~ U(-1,1), against the
+    # oracle within tolerance, and the same bits on a second run.
     import torch
     from cudair import kernels
-    M, N, K = 16, 14336, 4096
+    N, K = 14336, 4096
     a16, af = _seeded_normal_f16(oracle, M * K, 9, 1.0)
     b16, bf = _seeded_normal_f16(oracle, K * N, 10, 0.02)
     c = oracle.uniform(M * N, 63).reshape(M, N)
@@ -111,10 +145,10 @@ def test_chunked_decode_shape_seeded(dev, cudair, oracle):
 def test_chunked_refuses_other_forms(dev, cudair):
     import torch
     from cudair import kernels
-    a = torch.zeros(33, 64, dtype=torch.float16, device=dev)
+    a = torch.zeros(65, 64, dtype=torch.float16, device=dev)
     b = torch.zeros(64, 128, dtype=torch.float16, device=dev)
-    c = torch.zeros(33, 128, dtype=torch.float32, device=dev)
-    with pytest.raises(Exception, match="M <= 32"):
+    c = torch.zeros(65, 128, dtype=torch.float32, device=dev)
+    with pytest.raises(Exception, match="M <= 64"):
         kernels.gemm(a, b, c)
     with pytest.raises(Exception, match="plain form"):
         kernels.gemm_ex(a[:16], b, c[:16], overwrite=True)
