@@ -1030,11 +1030,21 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
     return CUDAIR_OK;
 }
 
+// The automatic choice takes the chunked kernel up to this many rows (all the
+// kernel runs).  At 33 to 64 rows, chains of 30 launches against stream-K:
+// 64 x 14336 x 4096 32.3 against 34.0 us (S = 2), 33 x 14336 x 4096 28.2
+// against 30.9, 40 x 8192 x 8192 29.6 against 34.6, 64 x 4096 x 4096 16.6
+// against 21.8 (S = 4), 64 x 2048 x 8192 20.5 (S = 4) against 27.8.  With
+// more 128-column tiles than SMs it lost there (160, 192 and 256 tiles at
+// M = 64: 44.2, 48.1, 61.3 against 40.9, 46.9, 59.4 us), so above 32 rows
+// those shapes keep stream-K.
+constexpr int kChunkedAutoMaxM = skinny::CH_MAX_MPAD;
+
 // The automatic choice between the two few-row kernels, from measurements on
 // a B200 (148 SMs) of M = 1, 16 and 32 with N from 1024 to 57344 and K from
 // 4096 to 28672, each kernel in a chain of 20-30 launches with B requested
 // early.  Returns the chunks per n-tile for the chunked kernel, or 0 for the
-// stream-K kernel (M > 32, or K under four k-blocks per chunk).
+// stream-K kernel (M > 64, or K under four k-blocks per chunk).
 //   * At most half as many 128-column tiles as SMs: G / n_tiles chunks per
 //     tile, so every CTA runs one chunk and every tile has equal parts (8-16 %
 //     faster than stream-K at 8 to 64 tiles).
@@ -1045,9 +1055,6 @@ int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int
 //     the measured best, or one within 2 %, at every tile count from 80 to
 //     448; against stream-K it is 3-12 % faster, except at M = 32 with 160
 //     or 256 tiles (1-4 % slower).
-// The automatic choice takes the chunked kernel up to this many rows; the
-// kernel itself runs up to skinny::CH_MAX_MPAD (variant 6).
-constexpr int kChunkedAutoMaxM = 32;
 int chunked_auto_chunks(int M, int N, int K, int sm_count) {
     const int mpad = (M + 15) / 16 * 16;
     if (mpad > kChunkedAutoMaxM || sm_count < 2) return 0;
@@ -1058,6 +1065,7 @@ int chunked_auto_chunks(int M, int N, int K, int sm_count) {
         const long long S = std::min(G / n_tiles, max_s);
         return S >= 2 ? static_cast<int>(S) : 0;
     }
+    if (mpad > 32 && n_tiles > G) return 0;
     int best = 0;
     double best_fill = 0.0;
     for (long long S = 2; S <= (mpad <= 16 ? 4 : 3) && S <= max_s; ++S) {

@@ -194,9 +194,9 @@ int cudair_gemm(const void *a, const void *b, void *c, const float *bias,
  * Selects the GEMM kernel variant for subsequent calls in this process:
  * 0 = automatic (few-row kernel when M <= 64, and when M <= 128 with
  * N <= 8192, given one 128-column x 64-k unit of work per SM, in its
- * chunked form (6) for M <= 32 where the tile count fills the SMs with
+ * chunked form (6) for M <= 64 where the tile count fills the SMs with
  * whole waves of chunks, its stream-K form (3) otherwise; the chunked form
- * also for M <= 32 with fewer such units than SMs when K splits into at
+ * also for M <= 64 with fewer such units than SMs when K splits into at
  * least two chunks of four 64-k blocks (narrow N, long K); the
  * small-problem kernel when K <= 512 and its 128 x 64 tiles fit one wave;
  * single CTAs with 128 x 256 tiles for the rest of M <= 128; else CTA pairs

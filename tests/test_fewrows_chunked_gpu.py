@@ -154,11 +154,13 @@ def test_chunked_refuses_other_forms(dev, cudair):
         kernels.gemm_ex(a[:16], b, c[:16], overwrite=True)
 
 
-@pytest.mark.parametrize("M,N,K", [(16, 128, 4096), (1, 128, 8192), (32, 296, 2048), (7, 256, 1000)])
-def test_automatic_choice_narrow_long_k(dev, cudair, oracle, M, N, K):
-    # Fewer (128-column x 64-k) units than SMs at M <= 32: the automatic
+@pytest.mark.parametrize("M,N,K", [(16, 128, 4096), (1, 128, 8192), (32, 296, 2048), (7, 256, 1000),
+                                   (64, 128, 4096), (48, 256, 2048), (64, 4096, 4096), (40, 2048, 2048)])
+def test_automatic_choice_takes_chunked(dev, cudair, oracle, M, N, K):
+    # Fewer (128-column x 64-k) units than SMs at M <= 64: the automatic
     # choice cuts K into chunks on the chunked kernel instead of streaming all
-    # of K through one SM.  Exact on the integer generator; on seeded data the
+    # of K through one SM; with more units at 33 to 64 rows it also takes the
+    # chunked kernel.  Exact on the integer generator; on seeded data the
     # same bits as the chunked kernel chosen explicitly (so that kernel ran)
     # and within the oracle's tolerance.
     import torch

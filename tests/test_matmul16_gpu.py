@@ -38,7 +38,7 @@ def variant(request, dev, cudair):
     """Runs a test on each GEMM kernel in turn: single CTA (128x256 tiles),
     CTA pair (256x256), the few-row kernel (M <= 128), the wide CTA pair
     (256x512), the small-problem kernel (K <= 512, one 128x64 tile per CTA)
-    and the chunked few-row kernel (M <= 32), then restores the automatic
+    and the chunked few-row kernel (M <= 64), then restores the automatic
     choice."""
     from cudair import kernels
     kernels.set_gemm_variant(request.param)
@@ -51,8 +51,8 @@ def _applies(variant, M, K=0):
         pytest.skip("the few-row kernel takes M <= 128")
     if variant == 5 and K > 512:
         pytest.skip("the small-problem kernel takes K <= 512")
-    if variant == 6 and M > 32:
-        pytest.skip("the chunked few-row kernel takes M <= 32")
+    if variant == 6 and M > 64:
+        pytest.skip("the chunked few-row kernel takes M <= 64")
 
 
 def kat(M, N, K):
