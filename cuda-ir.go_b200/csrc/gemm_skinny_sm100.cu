@@ -1046,8 +1046,9 @@ constexpr int kChunkedAutoMaxM = skinny::CH_MAX_MPAD;
 // early.  Returns the chunks per n-tile for the chunked kernel, or 0 for the
 // stream-K kernel (M > 64, or K under four k-blocks per chunk).
 //   * At most half as many 128-column tiles as SMs: G / n_tiles chunks per
-//     tile, so every CTA runs one chunk and every tile has equal parts (8-16 %
-//     faster than stream-K at 8 to 64 tiles).
+//     tile (at most one per eight k-blocks), so every CTA runs at most one
+//     chunk and every tile has equal parts (8-16 % faster than stream-K at 8
+//     to 64 tiles).
 //   * More tiles: the chunks run in waves of G, and a wave that is only
 //     partly full leaves the HBM to fewer SMs.  The count S in 2..4 (2..3 at
 //     M > 16) whose waves are fullest, n_tiles * S / (ceil(n_tiles * S / G) * G),
@@ -1062,7 +1063,11 @@ int chunked_auto_chunks(int M, int N, int K, int sm_count) {
     const long long n_tiles = (N + skinny::BN_T - 1) / skinny::BN_T;
     const long long max_s = ((K + skinny::BK - 1) / skinny::BK) / 4;  // chunks of at least four k-blocks
     if (2 * n_tiles <= G) {
-        const long long S = std::min(G / n_tiles, max_s);
+        // Chunks of at least eight k-blocks here: shorter ones cost more in
+        // their parts' sum than they gain in SMs (16 x 128 x 4096: 8.65 us
+        // with 8 chunks, 9.1 with 16; 64 x 128 x 4096: 15.2 against 20.5;
+        // 32 x 296 x 2048: 9.5 with 4 chunks against 9.9 with 8).
+        const long long S = std::min(G / n_tiles, static_cast<long long>((K + skinny::BK - 1) / skinny::BK) / 8);
         return S >= 2 ? static_cast<int>(S) : 0;
     }
     if (mpad > 32 && n_tiles > G) return 0;

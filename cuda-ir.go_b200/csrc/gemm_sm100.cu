@@ -1035,10 +1035,10 @@ int gemm_launch(const void *a, const void *b, void *c, int64_t M, int64_t N, int
     const int use_variant = small_auto ? 5 : variant;
     // Fewer units than SMs at M <= 64 (narrow N, long K: a single-CTA tile
     // would stream all of K on one SM) take the chunked kernel when its rule
-    // splits K into at least two chunks of four or more k-blocks, one chunk
-    // per CTA (16 x 128 x 4096: 9.0 us against 21.2 us; 1 x 128 x 8192:
-    // 11.3 against 39.4 us; 32 x 256 x 2048: 9.8 against 16.4 us, chains of
-    // 30 launches).
+    // splits K into at least two chunks of eight or more k-blocks, one chunk
+    // per CTA (chains of 30 launches: 16 x 128 x 4096 8.65 us against 21.2
+    // us; 64 x 128 x 4096 15.2 against 21.3 us; 48 x 512 x 2048 11.0
+    // against 16.4 us).
     const bool few_units = variant == 0 && flags == 0 && !small_auto && M <= 64 && units < dev->sm_count;
     // The few-row kernels: with fixed k-chunks handed out at run time where
     // that measured faster (chunked_auto_chunks), else stream-K.

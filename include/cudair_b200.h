@@ -197,7 +197,7 @@ int cudair_gemm(const void *a, const void *b, void *c, const float *bias,
  * chunked form (6) for M <= 64 where the tile count fills the SMs with
  * whole waves of chunks, its stream-K form (3) otherwise; the chunked form
  * also for M <= 64 with fewer such units than SMs when K splits into at
- * least two chunks of four 64-k blocks (narrow N, long K); the
+ * least two chunks of eight 64-k blocks (narrow N, long K); the
  * small-problem kernel when K <= 512 and its 128 x 64 tiles fit one wave;
  * single CTAs with 128 x 256 tiles for the rest of M <= 128; else CTA pairs
  * with 256 x 256 or 256 x 512 tiles, whichever a makespan estimate for the
