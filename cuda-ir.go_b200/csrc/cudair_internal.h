@@ -74,7 +74,7 @@ int wait_status_current_device(unsigned int **status);
 int gemm_skinny_launch(const void *a, const void *b, float *c, int M, int N, int K, int64_t lda,
                        int64_t ldb, int64_t ldc, int sm_count, unsigned int *status,
                        cudaStream_t stream);
-// The chunked few-row variant (M <= 32): fixed k-chunks per n-tile handed
+// The chunked few-row variant (M <= 64): fixed k-chunks per n-tile handed
 // out at run time; same operands and result rules as gemm_skinny_launch.
 // chunks > 0 sets the chunks per n-tile, 0 picks them automatically.
 int gemm_chunked_launch(const void *a, const void *b, float *c, int M, int N, int K, int64_t lda,

@@ -27,7 +27,7 @@
 // owner and MMA issuer, warps 2-5 epilogue and fix-up.  All waits are
 // bounded.
 //
-// A second kernel below (gemm_chunked_kernel, M <= 32) keeps the swap of
+// A second kernel below (gemm_chunked_kernel, M <= 64) keeps the swap of
 // operands and the ring but replaces the static ranges by fixed k-chunks
 // that the CTAs take at run time; chunked_auto_chunks picks it for the
 // shapes where it measured faster.
