@@ -1066,8 +1066,12 @@ int chunked_auto_chunks(int M, int N, int K, int sm_count) {
         // Chunks of at least eight k-blocks here: shorter ones cost more in
         // their parts' sum than they gain in SMs (16 x 128 x 4096: 8.65 us
         // with 8 chunks, 9.1 with 16; 64 x 128 x 4096: 15.2 against 20.5;
-        // 32 x 296 x 2048: 9.5 with 4 chunks against 9.9 with 8).
-        const long long S = std::min(G / n_tiles, static_cast<long long>((K + skinny::BK - 1) / skinny::BK) / 8);
+        // 32 x 296 x 2048: 9.5 with 4 chunks against 9.9 with 8).  Above
+        // four, a multiple of four: the tile's sum loads the parts four at a
+        // time (1 x 1024 x 16384: 13.7 us with 16 chunks, 15.3 with 18;
+        // 16 x 2048 x 8192: 11.9 with 8, 13.6 with 9).
+        long long S = std::min(G / n_tiles, static_cast<long long>((K + skinny::BK - 1) / skinny::BK) / 8);
+        if (S > 4) S -= S % 4;
         return S >= 2 ? static_cast<int>(S) : 0;
     }
     if (mpad > 32 && n_tiles > G) return 0;
